@@ -1,0 +1,126 @@
+/*
+ * pagedbatch_b200 — C ABI of the B200 (sm_100a) batched token sampler.
+ *
+ * This library replaces the per-row sampling call of pagedbatch:
+ *   pagedbatch/sampling.py:10   sample_token(logits[V], params, generator) -> int
+ * which the engine calls once per scheduled row:
+ *   pagedbatch/engine.py:133-139 (LLMEngine._postprocess)
+ * with one launch over a whole batch of rows [n_rows, vocab]. The per-request knobs are those of
+ *   pagedbatch/config.py:134-158 (SamplingParams: temperature, top_p, top_k; greedy <=> temperature == 0).
+ *
+ * Plain C types only: device pointers, sizes and a cudaStream_t passed as void*. Every entry
+ * point returns 0 on success or a negative PB_E* code; none aborts, none synchronises the
+ * stream, none allocates device memory.
+ *
+ * Sampling semantics (exact, integer where it can be):
+ *   key_j  = fp32(logit_j) / fp32(temperature)          IEEE fp32 division   (sampling.py:14)
+ *   order  = keys descending, ties by index ascending
+ *   top-k  (0 < k < vocab): keep every key >= the k-th largest key (ties kept)  (sampling.py:15-17)
+ *   w_j    = pb_exp(fp32(key_j - max_key)), q_j = floor(w_j * 2^40)   (fixed-point weights)
+ *   top-p  (top_p < 1): keep position j iff sum_{i<j} q_i <= floor(fp32(top_p) * sum_K q)  (sampling.py:18-25)
+ *   draw   : t = floor(U53 * sum_S q / 2^53), U53 = uniform * 2^53; token = first position in
+ *            `order` (restricted to the kept set S) whose inclusive prefix of q exceeds t.
+ *            This is an inverse-CDF draw; the reference draws with torch.multinomial (sampling.py:26-27).
+ *   greedy : argmax of the raw logits, lowest index on ties                     (sampling.py:12-13)
+ */
+#ifndef PAGEDBATCH_B200_H
+#define PAGEDBATCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PB_API __attribute__((visibility("default")))
+#else
+#define PB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- dtypes of the logits buffer ------------------------------------------------------- */
+#define PB_DTYPE_F32 0
+#define PB_DTYPE_BF16 1
+#define PB_DTYPE_F16 2
+
+/* ---- return codes ---------------------------------------------------------------------- */
+#define PB_OK 0
+#define PB_E_INVALID (-1)    /* bad argument: null pointer, size, dtype, stride, alignment */
+#define PB_E_TOO_LARGE (-2)  /* vocab >= PB_MAX_VOCAB */
+#define PB_E_LAUNCH (-3)     /* the CUDA launch failed (cudaGetLastError after the launch) */
+#define PB_E_DEVICE (-4)     /* no usable sm_100 device / attribute query failed */
+
+/* Largest vocabulary: sums of 2^40-scaled weights must fit in 64 bits. */
+#define PB_MAX_VOCAB (1 << 24)
+
+/* ---- per-row status (pb_row_info.status; the row's token is then -1) -------------------- */
+#define PB_ROW_OK 0
+#define PB_ROW_NONFINITE 1   /* max key is +inf/NaN or every key is -inf: the reference's
+                                torch.multinomial raises on such rows (sampling.py:27) */
+#define PB_ROW_BAD_UNIFORM 2 /* uniform outside [0, 1) */
+#define PB_ROW_TIMEOUT 4     /* a bounded wait on a bulk copy gave up; outputs are not valid */
+#define PB_ROW_INTERNAL 8    /* a selection found no element for its target (an internal error) */
+
+/* pb_row_info.flags: which path resolved the row (diagnostic) */
+#define PB_PATH_GREEDY 1
+#define PB_PATH_SMALL 2      /* top-k candidates resolved in shared memory */
+#define PB_PATH_LARGE 4      /* cluster-cooperative histogram selection over the row */
+
+/* One row's sampling parameters (SamplingParams, config.py:134-158, plus the row's draw). */
+typedef struct pb_row_params {
+  double temperature; /* 0 => greedy (config.py:156-158); else the row is divided by fp32(temperature) */
+  double top_p;       /* (0, 1]; active iff top_p < 1.0 (sampling.py:18) */
+  double uniform;     /* [0, 1) draw for the inverse CDF; ignored for greedy rows */
+  int32_t top_k;      /* active iff 0 < top_k < vocab (sampling.py:15) */
+  int32_t reserved;   /* must be 0 */
+} pb_row_params;
+
+/* What the sampler decided for one row (optional output; used by the parity tests). */
+typedef struct pb_row_info {
+  uint32_t thr_key;   /* order-preserving key of the last kept position */
+  int32_t n_tie_kept; /* kept elements whose key equals thr_key (lowest indices first) */
+  int32_t kept_count; /* number of kept positions */
+  int32_t status;     /* PB_ROW_* */
+  float max_key;      /* largest scaled key (raw logit for greedy rows) */
+  int32_t flags;      /* PB_PATH_* */
+  uint64_t z_q;       /* sum of q over the top-k survivors K */
+  uint64_t kept_q;    /* sum of q over the kept set S */
+} pb_row_info;
+
+/*
+ * Sample one token for each of n_rows rows, in one launch on `stream`.
+ *
+ * Replaces: pagedbatch/sampling.py:10-27 sample_token, called per row at pagedbatch/engine.py:139.
+ *
+ *   logits      device, dtype `dtype`, row r at logits + r*row_stride elements, last dim contiguous.
+ *   row_index   optional device int32[n_rows]: work item i samples logits row row_index[i]
+ *               (lets the engine skip rows whose samples_token is False, engine.py:136-137).
+ *   params      device pb_row_params[n_rows].
+ *   out_token   device int64[n_rows]; -1 for a row whose status is not PB_ROW_OK.
+ *   out_info    optional device pb_row_info[n_rows].
+ *   out_probs   optional device float[n_rows * vocab]: the renormalised probabilities of the
+ *               final distribution (sampling.py:26), zero outside the kept set.
+ *   stream      cudaStream_t.
+ */
+PB_API int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                     const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
+                     pb_row_info* out_info, float* out_probs, void* stream);
+
+/* Order-preserving 32-bit key of a float (NaN above +inf, -0 == +0); host helper for tests. */
+PB_API uint32_t pb_key_of(float x);
+
+/* The fixed exp of the weights, w = pb_exp(d) for d <= 0 (host copy of the device function). */
+PB_API float pb_exp(float d);
+
+/* Short text for a PB_E* code. */
+PB_API const char* pb_strerror(int code);
+
+/* Version of this library, as major*10000 + minor*100 + patch. */
+PB_API int pb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEDBATCH_B200_H */

@@ -1,0 +1,1387 @@
+// B200 (sm_100a) batched token sampler: greedy / temperature / top-k / top-p with an
+// inverse-CDF draw, one thread-block cluster per logits row, every row of a batch in one launch.
+//
+// Replaces pagedbatch/sampling.py:10-27 (sample_token), called per row by
+// pagedbatch/engine.py:133-139. Exact semantics are stated in include/pagedbatch_b200.h.
+//
+// Per row (cluster of C CTAs, each owning a contiguous slice of the row):
+//  1. Stream: the slice goes HBM -> shared memory through a ring of 1-D bulk copies (TMA engine,
+//     mbarrier completion, no multicast). Each element becomes key = x / T (IEEE fp32); the CTA
+//     keeps the max key (lowest index on ties) and, for top-k rows with k <= KSMALL, a candidate
+//     list of keys >= a running threshold (the k-th largest key seen so far: a lower bound of the
+//     row's k-th key, so no survivor is ever dropped).
+//  2. Greedy rows finish here. Small top-k rows finish in rank 0's shared memory: exact k-th key
+//     by radix select over the candidates of all C CTAs (read through distributed shared memory),
+//     the survivors sorted by (key desc, index asc), fixed-point weights scanned for the top-p
+//     cut and the draw.
+//  3. Other rows (temperature-only, top-p over the full vocabulary, large k): the cluster re-reads
+//     its slices (L2) in histogram passes. Pass Z bins the fixed-point weight mass by distance to
+//     the max; each selection (k-th key, top-p cut, draw) walks down from the bin holding its
+//     target, either gathering the bin's elements into rank 0 for an exact finish or refining by
+//     11-bit digits of the key; a tie group larger than the gather buffer is resolved by counting.
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+
+#include "../../include/pagedbatch_b200.h"
+#include "pb_device.cuh"
+
+namespace cg = cooperative_groups;
+using namespace pb;
+
+namespace {
+
+constexpr int NT = 256;             // threads per CTA
+constexpr int NW = NT / 32;
+constexpr int CHUNK_ELEMS = 2048;   // elements per staged chunk
+constexpr int NSTAGE = 4;           // chunks in flight per CTA
+constexpr int CAND_CAP = 4096;      // candidate entries per CTA
+constexpr int CAND_HI = 2048;       // compaction trigger (CAND_CAP - CHUNK_ELEMS)
+constexpr int KSMALL = 1024;        // largest top_k resolved from the streamed candidates
+constexpr int KCAP = 4096;          // survivors of the small path sorted in rank 0
+constexpr int NBIN = 2048;          // histogram bins of the cooperative selection
+constexpr int GCAP = 4096;          // elements gathered into rank 0 for an exact finish
+constexpr int WAIT_POLLS = 20000;   // bounded mbarrier wait (~seconds) before a row reports a timeout
+constexpr float MASS_RANGE = 27.75f;  // below max - 27.75 the 2^40-scaled weight is 0
+
+static_assert(CAND_HI + CHUNK_ELEMS <= CAND_CAP, "a chunk must fit after the trigger level");
+
+// dynamic shared memory regions (bytes)
+constexpr int REGION_A = 32768;  // ring | local histograms | small-path survivors
+constexpr int REGION_B = 32768;  // candidates | gather list (rank 0)
+constexpr int REGION_C = NBIN * 8 + NBIN * 4;  // reduced level-1 histogram (rank 0)
+constexpr int DYN_SMEM = REGION_A + REGION_B + REGION_C;
+
+struct Args {
+  const char* logits;
+  int64_t n_rows, vocab, row_stride;
+  const int32_t* row_index;
+  const pb_row_params* params;
+  int64_t* out_token;
+  pb_row_info* out_info;
+  float* out_probs;
+};
+
+// decision record broadcast by rank 0 (read by peers through DSMEM)
+struct Dec {
+  uint32_t lo, hi;       // current key interval of the selection
+  uint64_t above_w;      // weight strictly above the interval
+  uint64_t above_c;      // count strictly above the interval
+  uint64_t cnt;          // elements in the interval
+  uint64_t w_in;         // weight in the interval
+  int32_t action;        // what the next pass does
+  int32_t shift;         // digit shift of a refinement pass
+  uint32_t res_key;      // result key
+  int32_t res_idx;       // result index (or -1)
+  uint64_t res_above_w;  // weight strictly above res_key
+  uint64_t res_above_c;  // count strictly above res_key
+  uint64_t res_cnt_at;   // elements equal to res_key (in the selection's set)
+  uint64_t res_w_at;     // weight of one element equal to res_key
+  uint64_t aux;          // extra result (rank of the draw inside a tie group, ...)
+  int32_t fail;          // no element found for the target (internal error)
+};
+
+enum : int32_t { ACT_DONE = 0, ACT_GATHER = 1, ACT_REFINE = 2, ACT_TIE = 3 };
+enum : int { MODE_COUNT = 0, MODE_MASS = 1 };
+
+struct Shared {
+  uint64_t mbar[NSTAGE];
+  // row parameters
+  double temperature, top_p, uniform;
+  int32_t top_k, greedy, filtering, status;
+  float tf;
+  int64_t row;
+  // stage-1 state
+  int32_t cand_n, overflow, timeout;
+  uint32_t thr;
+  // published per-CTA stage-1 results (read by the other CTAs of the cluster)
+  uint32_t pub_key, pub_idx, pub_min;
+  int32_t pub_cand_n, pub_overflow, pub_timeout;
+  // cluster-wide row facts (identical in every CTA)
+  uint32_t mk, arg, kmin;
+  int32_t any_overflow, any_timeout;
+  // gather list control (rank 0)
+  int32_t g_n;
+  int32_t nk;
+  // decisions
+  Dec dec;        // written by rank 0
+  Dec dec_local;  // every CTA's copy of rank 0's dec
+  // scratch for scans and reductions
+  uint64_t s64[NW + 2];
+  uint32_t s32[NW + 2];
+  uint32_t sel_digit, sel_kk;
+  int32_t found_pos;
+  uint64_t found_incl;
+  uint32_t hist256[256];
+};
+
+template <typename T>
+struct Elem;
+template <>
+struct Elem<float> {
+  static constexpr int ES = 4, EPV = 4;
+  __device__ static float ld(const float* p) { return __ldg(p); }
+  __device__ static void unpack(uint4 v, float* x) {
+    x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y);
+    x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
+  }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int ES = 2, EPV = 8;
+  __device__ static float ld(const __nv_bfloat16* p) {
+    return __uint_as_float(((uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p))) << 16);
+  }
+  __device__ static void unpack(uint4 v, float* x) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+};
+template <>
+struct Elem<__half> {
+  static constexpr int ES = 2, EPV = 8;
+  __device__ static float ld(const __half* p) { return __half2float(__ldg(p)); }
+  __device__ static void unpack(uint4 v, float* x) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xFFFF)));
+      x[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+    }
+  }
+};
+
+// This CTA's part of the row: scalar head (rank 0), 16-byte vectors, scalar tail (last rank).
+struct Slice {
+  int64_t head_n;    // elements [0, head_n) loaded one by one (rank 0 only, else 0)
+  int64_t vec_e0;    // first element of this CTA's vectors
+  int64_t nvec;      // number of 16-byte vectors
+  int64_t tail_e0;   // first tail element (last rank only)
+  int64_t tail_n;    // tail elements
+  int64_t e_lo, e_hi;  // element range of the whole slice
+};
+
+template <typename T>
+__device__ Slice make_slice(const T* row, int64_t V, int rank, int C) {
+  constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(row);
+  int64_t head = (int64_t)(((16 - (a0 & 15)) & 15) / ES);
+  if (head > V) head = V;
+  const int64_t nvec_all = (V - head) / EPV;
+  const int64_t tail0 = head + nvec_all * EPV;
+  const int64_t base = nvec_all / C, rem = nvec_all % C;
+  const int64_t v0 = rank * base + (rank < rem ? rank : rem);
+  Slice s;
+  s.nvec = base + (rank < rem ? 1 : 0);
+  s.vec_e0 = head + v0 * EPV;
+  s.head_n = (rank == 0) ? head : 0;
+  s.tail_e0 = tail0;
+  s.tail_n = (rank == C - 1) ? (V - tail0) : 0;
+  s.e_lo = (rank == 0) ? 0 : s.vec_e0;
+  s.e_hi = (rank == C - 1) ? V : s.vec_e0 + s.nvec * EPV;
+  return s;
+}
+
+// Visit every element of the slice (any order per thread; no warp-collective work in f).
+template <typename T, typename F>
+__device__ __forceinline__ void for_slice(const T* row, const Slice& s, F&& f) {
+  constexpr int EPV = Elem<T>::EPV;
+  for (int64_t e = threadIdx.x; e < s.head_n; e += NT) f(Elem<T>::ld(row + e), (uint32_t)e);
+  const uint4* vp = reinterpret_cast<const uint4*>(row + s.vec_e0);
+  for (int64_t v = threadIdx.x; v < s.nvec; v += NT) {
+    float x[EPV];
+    Elem<T>::unpack(__ldg(vp + v), x);
+    const uint32_t e0 = (uint32_t)(s.vec_e0 + v * EPV);
+#pragma unroll
+    for (int j = 0; j < EPV; ++j) f(x[j], e0 + j);
+  }
+  for (int64_t e = threadIdx.x; e < s.tail_n; e += NT) f(Elem<T>::ld(row + s.tail_e0 + e), (uint32_t)(s.tail_e0 + e));
+}
+
+// Visit the slice in index order: tiles of NT consecutive vectors (or scalars for head and tail);
+// f(x, e, pred) returns the predicate; g(e, rank_before) is called for every element whose
+// predicate holds, with the number of such elements before it in this slice (index order).
+template <typename T, typename P, typename G>
+__device__ void ordered_slice(const T* row, const Slice& s, Shared& sh, P&& pred, G&& g) {
+  constexpr int EPV = Elem<T>::EPV;
+  uint32_t run = 0;
+  auto scalar_part = [&](int64_t e0, int64_t n) {
+    for (int64_t t0 = 0; t0 < n; t0 += NT) {
+      const int64_t e = e0 + t0 + threadIdx.x;
+      const bool in = (t0 + threadIdx.x) < n;
+      float x = in ? Elem<T>::ld(row + e) : 0.0f;
+      const uint32_t c = (in && pred(x, (uint32_t)e)) ? 1u : 0u;
+      uint32_t tot;
+      const uint32_t ex = block_excl_scan<uint32_t, NT>(c, sh.s32, &tot);
+      if (c) g(x, (uint32_t)e, run + ex);
+      run += tot;
+    }
+  };
+  scalar_part(0, s.head_n);
+  const uint4* vp = reinterpret_cast<const uint4*>(row + s.vec_e0);
+  for (int64_t t0 = 0; t0 < s.nvec; t0 += NT) {
+    const int64_t v = t0 + threadIdx.x;
+    float x[EPV];
+    bool pr[EPV];
+    uint32_t c = 0;
+    const uint32_t e0 = (uint32_t)(s.vec_e0 + v * EPV);
+    if (v < s.nvec) {
+      Elem<T>::unpack(__ldg(vp + v), x);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) {
+        pr[j] = pred(x[j], e0 + j);
+        c += pr[j] ? 1u : 0u;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) pr[j] = false;
+    }
+    uint32_t tot;
+    uint32_t ex = block_excl_scan<uint32_t, NT>(c, sh.s32, &tot);
+    if (c) {
+#pragma unroll
+      for (int j = 0; j < EPV; ++j)
+        if (pr[j]) g(x[j], e0 + j, run + ex++);
+    }
+    run += tot;
+  }
+  scalar_part(s.tail_e0, s.tail_n);
+}
+
+// Warp-aggregated append of (key, idx) to a shared list; all 32 lanes must call.
+__device__ __forceinline__ void warp_append(bool pass, uint32_t key, uint32_t idx, uint64_t* list, int32_t* cnt,
+                                            int cap) {
+  const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
+  if (m == 0) return;
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(m) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(cnt, __popc(m));
+  base = __shfl_sync(0xFFFFFFFFu, base, leader);
+  if (pass) {
+    const int pos = base + __popc(m & lanemask_lt());
+    if (pos < cap) list[pos] = compose(key, idx);
+  }
+}
+
+// k-th largest key (1 <= k <= total entries) over up to 8 lists of composites; all threads call.
+__device__ uint32_t block_kth_key(uint64_t* const* lists, const int32_t* counts, int nlists, int k, Shared& sh) {
+  uint32_t prefix = 0, mask = 0;
+  uint32_t kk = (uint32_t)k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += NT) sh.hist256[i] = 0;
+    __syncthreads();
+    for (int l = 0; l < nlists; ++l) {
+      const uint64_t* L = lists[l];
+      for (int i = threadIdx.x; i < counts[l]; i += NT) {
+        const uint32_t key = comp_key(L[i]);
+        if ((key & mask) == prefix) atomicAdd(&sh.hist256[(key >> shift) & 255], 1u);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = sh.hist256[255 - lane * 8 - j];
+        sum += c[j];
+      }
+      const uint32_t incl = warp_incl_scan(sum);
+      const uint32_t excl = incl - sum;
+      if (excl < kk && kk <= incl) {
+        uint32_t r = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (r + c[j] >= kk) {
+            sh.sel_digit = 255 - lane * 8 - j;
+            sh.sel_kk = kk - r;
+            break;
+          }
+          r += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= sh.sel_digit << shift;
+    mask |= 0xFFu << shift;
+    kk = sh.sel_kk;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Sort up to 4096 composites descending (bitonic network in shared memory); all threads call.
+__device__ void block_sort_desc(uint64_t* a, int n) {
+  int N = 2;
+  while (N < n) N <<= 1;
+  for (int i = n + threadIdx.x; i < N; i += NT) a[i] = 0;  // pads sort last
+  __syncthreads();
+  for (int k = 2; k <= N; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < (N >> 1); i += NT) {
+        const int lo = 2 * i - (i & (j - 1));
+        const int hi = lo + j;
+        const uint64_t x = a[lo], y = a[hi];
+        const bool desc = (lo & k) == 0;
+        if (desc ? (x < y) : (x > y)) {
+          a[lo] = y;
+          a[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Over a sorted list a[0..n): weights q (mode MASS) or 1 (mode COUNT); find the first position whose
+// inclusive prefix (plus `base`) exceeds `target`. Writes sh.found_pos / sh.found_incl
+// (found_incl = base + inclusive prefix at the position). All threads call.
+__device__ void list_find(const uint64_t* a, int n, int mode, float m, uint64_t base, uint64_t target, Shared& sh) {
+  const int seg = (n + NT - 1) / NT;
+  const int p0 = min(n, (int)threadIdx.x * seg), p1 = min(n, p0 + seg);
+  uint64_t sum = 0;
+  for (int p = p0; p < p1; ++p) sum += (mode == MODE_MASS) ? weight_q(value_of(comp_key(a[p])), m) : 1ull;
+  uint64_t tot;
+  const uint64_t ex = block_excl_scan<uint64_t, NT>(sum, sh.s64, &tot);
+  if (threadIdx.x == 0) sh.found_pos = -1;
+  __syncthreads();
+  const uint64_t lo = base + ex;
+  if (lo <= target && target < lo + sum) {
+    uint64_t run = lo;
+    for (int p = p0; p < p1; ++p) {
+      run += (mode == MODE_MASS) ? weight_q(value_of(comp_key(a[p])), m) : 1ull;
+      if (run > target) {
+        sh.found_pos = p;
+        sh.found_incl = run;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// first position p in sorted a[0..n) with comp_key(a[p]) == key (keys descending); single thread
+__device__ int first_of_key(const uint64_t* a, int n, uint32_t key) {
+  int lo = 0, hi = n;  // first p with comp_key(a[p]) <= key
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (comp_key(a[mid]) > key) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// level-1 bin of a key: distance below the max, scaled; non-increasing in the key
+__device__ __forceinline__ int bin_of(float key, float m, float scale) {
+  const float v = __fmul_rn(-__fsub_rn(key, m), scale);
+  return (v < (float)NBIN) ? (int)v : NBIN - 1;
+}
+__device__ __forceinline__ int bin_of_key(uint32_t k, float m, float scale) { return bin_of(value_of(k), m, scale); }
+
+// key interval [lo, hi] (within [0, mk]) of level-1 bin b
+__device__ void bin_interval(int b, uint32_t mk, float m, float scale, uint32_t* lo, uint32_t* hi) {
+  auto first_le = [&](int bb) -> uint32_t {  // smallest key in [0, mk] whose bin <= bb
+    uint32_t a = 0, z = mk;
+    while (a < z) {
+      const uint32_t mid = a + ((z - a) >> 1);
+      if (bin_of_key(mid, m, scale) <= bb) z = mid;
+      else a = mid + 1;
+    }
+    return a;
+  };
+  *lo = first_le(b);
+  *hi = (b == 0) ? mk : first_le(b - 1) - 1;
+}
+
+// ---- cluster helpers ------------------------------------------------------------------------
+
+__device__ __forceinline__ void pull_dec(cg::cluster_group& cluster, Shared& sh) {
+  if (threadIdx.x == 0) {
+    const Dec* d = cluster.map_shared_rank(&sh.dec, 0);
+    sh.dec_local = *d;
+  }
+  __syncthreads();
+}
+
+// Rank 0 sums the C CTAs' histograms into its own (hq/hc) and finds the bin whose inclusive
+// prefix of weight exceeds `target`. Weight = hq (MASS) or hc (COUNT). All rank-0 threads call.
+__device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq, uint32_t* hc, uint64_t* out_q,
+                                uint32_t* out_c, int nbins, int mode, uint64_t target, Shared& sh, int* b_out,
+                                uint64_t* above_w, uint64_t* above_c, uint64_t* bin_w, uint64_t* bin_c) {
+  for (int b = threadIdx.x; b < nbins; b += NT) {
+    uint64_t q = 0;
+    uint32_t c = 0;
+    for (int r = 0; r < C; ++r) {
+      const uint64_t* rq = cluster.map_shared_rank(hq, r);
+      const uint32_t* rc = cluster.map_shared_rank(hc, r);
+      if (mode == MODE_MASS) q += rq[b];
+      c += rc[b];
+    }
+    out_q[b] = (mode == MODE_MASS) ? q : (uint64_t)c;
+    out_c[b] = c;
+  }
+  __syncthreads();
+  const int per = (nbins + NT - 1) / NT;
+  const int b0 = min(nbins, (int)threadIdx.x * per), b1 = min(nbins, b0 + per);
+  uint64_t sw = 0, sc = 0;
+  for (int b = b0; b < b1; ++b) {
+    sw += out_q[b];
+    sc += out_c[b];
+  }
+  uint64_t tw, tc;
+  const uint64_t ew = block_excl_scan<uint64_t, NT>(sw, sh.s64, &tw);
+  const uint64_t ec = block_excl_scan<uint64_t, NT>(sc, sh.s64, &tc);
+  if (threadIdx.x == 0) sh.found_pos = -1;
+  __syncthreads();
+  if (ew <= target && target < ew + sw) {
+    uint64_t rw = ew, rc = ec;
+    for (int b = b0; b < b1; ++b) {
+      if (rw + out_q[b] > target) {
+        sh.found_pos = b;
+        sh.s64[NW + 1] = rw;  // above weight
+        sh.found_incl = rc;   // above count
+        break;
+      }
+      rw += out_q[b];
+      rc += out_c[b];
+    }
+  }
+  __syncthreads();
+  *b_out = sh.found_pos;
+  if (sh.found_pos >= 0) {
+    *above_w = sh.s64[NW + 1];
+    *above_c = sh.found_incl;
+    *bin_w = out_q[sh.found_pos];
+    *bin_c = out_c[sh.found_pos];
+  }
+  __syncthreads();
+}
+
+// ---- the kernel -------------------------------------------------------------------------
+
+template <typename T>
+__global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
+  constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
+  constexpr int CHUNK_VEC = CHUNK_ELEMS / EPV;
+  constexpr int VPT = CHUNK_VEC / NT;  // vectors per thread per chunk
+  static_assert(CHUNK_VEC % NT == 0, "chunk must split evenly");
+
+  extern __shared__ __align__(128) unsigned char dyn[];
+  __shared__ Shared sh;
+  unsigned char* regA = dyn;
+  uint64_t* candB = reinterpret_cast<uint64_t*>(dyn + REGION_A);
+  uint64_t* h1q = reinterpret_cast<uint64_t*>(dyn + REGION_A + REGION_B);
+  uint32_t* h1c = reinterpret_cast<uint32_t*>(dyn + REGION_A + REGION_B + NBIN * 8);
+  uint64_t* hq = reinterpret_cast<uint64_t*>(regA);
+  uint32_t* hc = reinterpret_cast<uint32_t*>(regA + NBIN * 8);
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  const int64_t item = blockIdx.x / C;
+  const int tid = threadIdx.x;
+  const int64_t V = a.vocab;
+
+  if (tid == 0) {
+    const pb_row_params p = a.params[item];
+    sh.temperature = p.temperature;
+    sh.top_p = p.top_p;
+    sh.uniform = p.uniform;
+    sh.top_k = p.top_k;
+    sh.greedy = (p.temperature == 0.0);
+    sh.tf = (float)p.temperature;
+    sh.filtering = !sh.greedy && p.top_k > 0 && (int64_t)p.top_k < V && p.top_k <= KSMALL;
+    sh.row = a.row_index ? (int64_t)a.row_index[item] : item;
+    sh.cand_n = 0;
+    sh.overflow = 0;
+    sh.timeout = 0;
+    sh.thr = 0;
+    sh.status = PB_ROW_OK;
+    for (int s = 0; s < NSTAGE; ++s) mbar_init(&sh.mbar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const bool greedy = sh.greedy;
+  const bool filtering = sh.filtering;
+  const float tf = sh.tf;
+  const int32_t top_k = sh.top_k;
+  const T* row = reinterpret_cast<const T*>(a.logits) + sh.row * a.row_stride;
+  const Slice s = make_slice(row, V, rank, C);
+
+  // ---------------- stage 1: stream the slice ----------------
+  uint32_t bk = 0, be = 0xFFFFFFFFu, mn = 0xFFFFFFFFu;
+  auto visit = [&](float x, uint32_t e, bool& pass) {
+    const float y = greedy ? x : __fdiv_rn(x, tf);
+    const uint32_t k = key_of(y);
+    if (k > bk || (k == bk && e < be)) {
+      bk = k;
+      be = e;
+    }
+    if (k > KEY_NEG_INF && k < mn) mn = k;
+    pass = filtering && k >= sh.thr;
+    return k;
+  };
+  auto compact = [&](int kth_rank) {
+    // keep the candidates whose key is >= the kth_rank-th largest
+    int32_t n = min(sh.cand_n, CAND_CAP);
+    uint64_t* lists[1] = {candB};
+    int32_t counts[1] = {n};
+    const uint32_t kth = block_kth_key(lists, counts, 1, kth_rank, sh);
+    uint64_t mine[CAND_CAP / NT];
+#pragma unroll
+    for (int j = 0; j < CAND_CAP / NT; ++j) {
+      const int i = j * NT + tid;
+      mine[j] = (i < n) ? candB[i] : 0ull;
+    }
+    __syncthreads();
+    if (tid == 0) sh.cand_n = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < CAND_CAP / NT; ++j) {
+      const bool keep = mine[j] != 0ull && comp_key(mine[j]) >= kth;
+      warp_append(keep, comp_key(mine[j]), comp_idx(mine[j]), candB, &sh.cand_n, CAND_CAP);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      sh.thr = kth;
+      if (sh.cand_n >= CAND_HI) sh.overflow = 1;  // ties hold the list above the trigger
+    }
+    __syncthreads();
+  };
+
+  // scalar head (rank 0): one element per thread, warp-uniform control flow
+  for (int64_t t0 = 0; t0 < s.head_n; t0 += NT) {
+    const int64_t e = t0 + tid;
+    bool pass = false;
+    uint32_t k = 0;
+    if (e < s.head_n) k = visit(Elem<T>::ld(row + e), (uint32_t)e, pass);
+    if (filtering) warp_append(pass, k, (uint32_t)e, candB, &sh.cand_n, CAND_CAP);
+  }
+  {
+    const int64_t nchunks = (s.nvec + CHUNK_VEC - 1) / CHUNK_VEC;
+    const uint4* src = reinterpret_cast<const uint4*>(row + s.vec_e0);
+    uint4* ring = reinterpret_cast<uint4*>(regA);
+    const bool keep_in_l2 = !greedy && !filtering;  // rows that re-read their slice
+    if (tid == 0) {
+      const uint64_t pol = keep_in_l2 ? l2_policy_evict_last() : l2_policy_evict_first();
+      for (int c = 0; c < NSTAGE && c < nchunks; ++c) {
+        const int64_t nv = min((int64_t)CHUNK_VEC, s.nvec - (int64_t)c * CHUNK_VEC);
+        mbar_expect_tx(&sh.mbar[c], (uint32_t)(nv * 16));
+        bulk_load(ring + c * CHUNK_VEC, src + (int64_t)c * CHUNK_VEC, (uint32_t)(nv * 16), &sh.mbar[c], pol);
+      }
+    }
+    for (int64_t c = 0; c < nchunks; ++c) {
+      const int stage = (int)(c % NSTAGE);
+      const uint32_t parity = (uint32_t)((c / NSTAGE) & 1);
+      if (!mbar_wait_bounded(&sh.mbar[stage], parity, WAIT_POLLS)) sh.timeout = 1;
+      __syncthreads();
+      if (sh.timeout) break;
+      const int64_t nv = min((int64_t)CHUNK_VEC, s.nvec - c * CHUNK_VEC);
+      const uint4* buf = ring + stage * CHUNK_VEC;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = j * NT + tid;
+        float x[EPV];
+        const bool valid = v < nv;
+        if (valid) Elem<T>::unpack(buf[v], x);
+        const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + v) * EPV);
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) {
+          bool pass = false;
+          uint32_t k = 0;
+          if (valid) k = visit(x[q], e0 + q, pass);
+          if (filtering) warp_append(pass, k, e0 + q, candB, &sh.cand_n, CAND_CAP);
+        }
+      }
+      __syncthreads();
+      if (tid == 0 && c + NSTAGE < nchunks) {
+        const uint64_t pol = keep_in_l2 ? l2_policy_evict_last() : l2_policy_evict_first();
+        const int64_t cn = c + NSTAGE;
+        const int64_t nv2 = min((int64_t)CHUNK_VEC, s.nvec - cn * CHUNK_VEC);
+        fence_proxy_async();
+        mbar_expect_tx(&sh.mbar[stage], (uint32_t)(nv2 * 16));
+        bulk_load(ring + stage * CHUNK_VEC, src + cn * CHUNK_VEC, (uint32_t)(nv2 * 16), &sh.mbar[stage], pol);
+      }
+      if (filtering && !sh.overflow && sh.cand_n >= CAND_HI) compact(top_k);
+    }
+    if (sh.timeout) {
+      // let every issued copy land before the shared memory is reused
+      if (tid == 0) {
+        const int64_t issued = nchunks;
+        for (int st = 0; st < NSTAGE; ++st) {
+          // last chunk issued on this stage, if any
+          int64_t last = -1;
+          for (int64_t c = st; c < issued; c += NSTAGE) last = c;
+          if (last >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((last / NSTAGE) & 1), WAIT_POLLS);
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int64_t t0 = 0; t0 < s.tail_n; t0 += NT) {
+    const int64_t e = s.tail_e0 + t0 + tid;
+    bool pass = false;
+    uint32_t k = 0;
+    if (t0 + tid < s.tail_n) k = visit(Elem<T>::ld(row + e), (uint32_t)e, pass);
+    if (filtering) warp_append(pass, k, (uint32_t)e, candB, &sh.cand_n, CAND_CAP);
+  }
+  __syncthreads();
+  if (filtering && !sh.overflow && sh.cand_n > CAND_CAP) sh.overflow = 1;
+  __syncthreads();
+  if (filtering && !sh.overflow && sh.cand_n > top_k) compact(top_k);
+
+  // CTA reduction of (max key, lowest index) and min key
+  {
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint32_t k2 = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
+      const uint32_t e2 = __shfl_xor_sync(0xFFFFFFFFu, be, o);
+      const uint32_t m2 = __shfl_xor_sync(0xFFFFFFFFu, mn, o);
+      if (k2 > bk || (k2 == bk && e2 < be)) {
+        bk = k2;
+        be = e2;
+      }
+      mn = min(mn, m2);
+    }
+    __shared__ uint32_t wk[NW], we[NW], wm[NW];
+    if ((tid & 31) == 0) {
+      wk[tid >> 5] = bk;
+      we[tid >> 5] = be;
+      wm[tid >> 5] = mn;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < NW; ++w) {
+        if (wk[w] > bk || (wk[w] == bk && we[w] < be)) {
+          bk = wk[w];
+          be = we[w];
+        }
+        mn = min(mn, wm[w]);
+      }
+      if (s.e_hi <= s.e_lo) {  // empty slice: neutral values
+        bk = 0;
+        be = 0xFFFFFFFFu;
+      }
+      sh.pub_key = bk;
+      sh.pub_idx = be;
+      sh.pub_min = mn;
+      sh.pub_cand_n = min(sh.cand_n, CAND_CAP);
+      sh.pub_overflow = sh.overflow;
+      sh.pub_timeout = sh.timeout;
+    }
+  }
+  cluster.sync();  // S1: stage-1 results visible cluster-wide
+
+  if (tid == 0) {
+    uint32_t mk = 0, arg = 0xFFFFFFFFu, kmin = 0xFFFFFFFFu;
+    int ov = 0, to = 0;
+    for (int r = 0; r < C; ++r) {
+      const Shared* p = cluster.map_shared_rank(&sh, r);
+      const uint32_t k = p->pub_key, e = p->pub_idx;
+      if (k > mk || (k == mk && e < arg)) {
+        mk = k;
+        arg = e;
+      }
+      kmin = min(kmin, p->pub_min);
+      ov |= p->pub_overflow;
+      to |= p->pub_timeout;
+    }
+    sh.mk = mk;
+    sh.arg = arg;
+    sh.kmin = kmin;
+    sh.any_overflow = ov;
+    sh.any_timeout = to;
+  }
+  __syncthreads();
+
+  const uint32_t mk = sh.mk;
+  const float m = value_of(mk);
+  float* prow = a.out_probs ? a.out_probs + item * V : nullptr;
+  pb_row_info info = {};
+  info.max_key = greedy ? value_of(mk) : m;
+  int64_t token = -1;
+  bool finished = false;
+
+  auto zero_probs = [&]() {
+    if (prow)
+      for (int64_t e = s.e_lo + tid; e < s.e_hi; e += NT) prow[e] = 0.0f;
+  };
+
+  if (sh.any_timeout) {
+    info.status = PB_ROW_TIMEOUT;
+    finished = true;
+  } else if (greedy) {
+    token = sh.arg;
+    info.thr_key = mk;
+    info.n_tie_kept = 1;
+    info.kept_count = 1;
+    info.flags = PB_PATH_GREEDY;
+    zero_probs();
+    cluster.sync();
+    if (prow && rank == 0 && tid == 0) prow[token] = 1.0f;
+    finished = true;
+  } else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) {
+    info.status = PB_ROW_NONFINITE;
+    finished = true;
+  } else if (!(sh.uniform >= 0.0 && sh.uniform < 1.0)) {
+    info.status = PB_ROW_BAD_UNIFORM;
+    finished = true;
+  }
+
+  const bool topp_active = sh.top_p < 1.0 && (float)sh.top_p < 1.0f;
+  const float pf = (float)sh.top_p;
+  const uint64_t u53 = (uint64_t)(sh.uniform * 0x1p53);
+
+  // ---------------- small path: survivors resolved in rank 0 ----------------
+  if (!finished && filtering && !sh.any_overflow) {
+    uint64_t* K = reinterpret_cast<uint64_t*>(regA);
+    zero_probs();
+    if (rank == 0) {
+      uint64_t* lists[8];
+      int32_t counts[8];
+      int32_t total = 0;
+      for (int r = 0; r < C; ++r) {
+        lists[r] = cluster.map_shared_rank(candB, r);
+        counts[r] = cluster.map_shared_rank(&sh, r)->pub_cand_n;
+        total += counts[r];
+      }
+      const uint32_t kth = block_kth_key(lists, counts, C, min(top_k, total), sh);
+      if (tid == 0) sh.nk = 0;
+      __syncthreads();
+      for (int r = 0; r < C; ++r) {
+        const uint64_t* L = lists[r];
+        for (int i0 = 0; i0 < counts[r]; i0 += NT) {
+          const int i = i0 + tid;
+          const uint64_t c = (i < counts[r]) ? L[i] : 0ull;
+          const bool keep = c != 0ull && comp_key(c) >= kth;
+          warp_append(keep, comp_key(c), comp_idx(c), K, &sh.nk, KCAP);
+        }
+      }
+      __syncthreads();
+      const int nk = sh.nk;
+      if (nk <= KCAP) {
+        block_sort_desc(K, nk);
+        uint64_t zq;
+        {
+          const int seg = (nk + NT - 1) / NT;
+          const int p0 = min(nk, tid * seg), p1 = min(nk, p0 + seg);
+          uint64_t sum = 0;
+          for (int p = p0; p < p1; ++p) sum += weight_q(value_of(comp_key(K[p])), m);
+          block_excl_scan<uint64_t, NT>(sum, sh.s64, &zq);
+        }
+        int last = nk - 1;
+        uint64_t kept = zq;
+        bool ok = true;
+        if (topp_active) {
+          list_find(K, nk, MODE_MASS, m, 0, mul_floor(pf, zq), sh);
+          last = sh.found_pos;
+          kept = sh.found_incl;
+          ok = last >= 0;
+        }
+        int pick = -1;
+        if (ok) {
+          list_find(K, nk, MODE_MASS, m, 0, scale_u53(u53, kept), sh);
+          pick = sh.found_pos;
+          ok = pick >= 0;
+        }
+        if (!ok) {
+          last = 0;
+          pick = 0;
+          info.status = PB_ROW_INTERNAL;
+        }
+        if (tid == 0) {
+          token = comp_idx(K[pick]);
+          const uint32_t tk = comp_key(K[last]);
+          info.thr_key = tk;
+          info.n_tie_kept = last - first_of_key(K, nk, tk) + 1;
+          info.kept_count = last + 1;
+          info.z_q = zq;
+          info.kept_q = kept;
+          info.flags = PB_PATH_SMALL;
+          sh.nk = nk;
+          sh.found_pos = last;
+          sh.s64[NW + 1] = kept;
+        }
+        __syncthreads();
+        if (tid == 0) sh.dec.action = ACT_DONE;
+      } else {
+        if (tid == 0) sh.dec.action = ACT_REFINE;  // too many survivors: cooperative path
+      }
+      __syncthreads();
+    }
+    cluster.sync();  // S2: rank 0 finished (or gave up); peers' zero-fill done
+    pull_dec(cluster, sh);
+    if (sh.dec_local.action == ACT_DONE) {
+      if (rank == 0 && prow) {
+        const int last = sh.found_pos;
+        const float zf = __fmul_rn(__ull2float_rn(sh.s64[NW + 1]), 0x1p-40f);
+        for (int p = tid; p <= last; p += NT) {
+          const float w = exp_weight(__fsub_rn(value_of(comp_key(K[p])), m));
+          prow[comp_idx(K[p])] = __fdiv_rn(w, zf);
+        }
+      }
+      finished = true;
+    }
+    cluster.sync();  // rank 0's gather/candidate buffers are free again
+  }
+
+  // ---------------- large path: cooperative histogram selection ----------------
+  if (!finished) {
+    info.flags = PB_PATH_LARGE;
+    uint64_t* G = candB;  // gather list (rank 0)
+    bool failed = false;
+
+    // One selection over the ordered set {key >= kfloor} (MASS: weight > 0 as well): find the
+    // element whose inclusive prefix (count or weight) first exceeds `target`. sh.dec_local holds
+    // the level-1 decision on entry and the result on exit. Every thread of every CTA calls.
+    auto select = [&](int mode, uint32_t kfloor, uint64_t target, bool need_index) {
+      for (int level = 0; level < 40; ++level) {
+        const Dec d = sh.dec_local;
+        if (d.action == ACT_DONE) break;
+        if (d.action == ACT_GATHER) {
+          if (rank == 0 && tid == 0) sh.g_n = 0;
+          cluster.sync();
+          int32_t* gn = cluster.map_shared_rank(&sh.g_n, 0);
+          uint64_t* g0 = cluster.map_shared_rank(G, 0);
+          for_slice<T>(row, s, [&](float x, uint32_t e) {
+            const uint32_t k = key_of(__fdiv_rn(x, tf));
+            if (k < d.lo || k > d.hi || k < kfloor) return;
+            if (mode == MODE_MASS && weight_q(value_of(k), m) == 0) return;
+            const int pos = atomicAdd(gn, 1);
+            if (pos < GCAP) g0[pos] = compose(k, e);
+          });
+          cluster.sync();
+          if (rank == 0) {
+            const int n = min(sh.g_n, GCAP);
+            block_sort_desc(G, n);
+            list_find(G, n, mode, m, (mode == MODE_MASS) ? d.above_w : d.above_c, target, sh);
+            if (tid == 0) {
+              Dec r = d;
+              r.action = ACT_DONE;
+              const int p = sh.found_pos;
+              if (p < 0 || sh.g_n > GCAP) {
+                r.fail = 1;
+                r.res_idx = -1;
+              } else {
+                const uint32_t rk = comp_key(G[p]);
+                const int f = first_of_key(G, n, rk);
+                int l = f;
+                while (l < n && comp_key(G[l]) == rk) ++l;
+                r.res_key = rk;
+                r.res_idx = (int32_t)comp_idx(G[p]);
+                r.res_w_at = (mode == MODE_MASS) ? weight_q(value_of(rk), m) : 1ull;
+                r.res_cnt_at = (uint64_t)(l - f);
+                r.res_above_c = d.above_c + (uint64_t)f;
+                uint64_t aw = d.above_w;
+                if (mode == MODE_MASS)
+                  for (int i = 0; i < f; ++i) aw += weight_q(value_of(comp_key(G[i])), m);
+                else
+                  aw = r.res_above_c;
+                r.res_above_w = aw;
+                r.aux = (uint64_t)(p - f);  // rank of the pick inside its tie group
+              }
+              sh.dec = r;
+            }
+            __syncthreads();
+          }
+          cluster.sync();
+          pull_dec(cluster, sh);
+          continue;
+        }
+        if (d.action == ACT_TIE) {
+          // one key holds the target and its tie group outgrows the gather buffer
+          const uint64_t wq = d.res_w_at;
+          const uint64_t base = (mode == MODE_MASS) ? d.above_w : d.above_c;
+          const uint64_t skip = (wq > 0 && target >= base) ? (target - base) / wq : 0;
+          if (rank == 0 && tid == 0) sh.g_n = -1;  // index not found yet
+          if (need_index) {
+            // per-CTA count of the key; slices are in index order by rank
+            if (tid == 0) sh.nk = 0;
+            __syncthreads();
+            uint32_t cnt = 0;
+            for_slice<T>(row, s, [&](float x, uint32_t) {
+              if (key_of(__fdiv_rn(x, tf)) == d.lo) cnt++;
+            });
+            cnt = warp_sum(cnt);
+            if ((tid & 31) == 0 && cnt) atomicAdd(&sh.nk, (int)cnt);
+            cluster.sync();
+            uint64_t before = 0;
+            for (int r = 0; r < rank; ++r) before += (uint64_t)cluster.map_shared_rank(&sh, r)->nk;
+            const uint64_t mine = (uint64_t)sh.nk;
+            const bool here = skip >= before && skip < before + mine;
+            if (here) {
+              const uint32_t want = (uint32_t)(skip - before);
+              int32_t* gidx = cluster.map_shared_rank(&sh.g_n, 0);
+              ordered_slice<T>(
+                  row, s, sh, [&](float x, uint32_t) { return key_of(__fdiv_rn(x, tf)) == d.lo; },
+                  [&](float, uint32_t e, uint32_t rnk) {
+                    if (rnk == want) *gidx = (int32_t)e;
+                  });
+            }
+          }
+          cluster.sync();
+          if (rank == 0 && tid == 0) {
+            Dec r = d;
+            r.action = ACT_DONE;
+            r.res_key = d.lo;
+            r.res_w_at = wq;
+            r.res_cnt_at = d.cnt;
+            r.res_above_w = d.above_w;
+            r.res_above_c = d.above_c;
+            r.aux = skip;
+            r.res_idx = need_index ? sh.g_n : -1;
+            if (need_index && sh.g_n < 0) r.fail = 1;
+            sh.dec = r;
+          }
+          cluster.sync();
+          pull_dec(cluster, sh);
+          continue;
+        }
+        // ACT_REFINE: histogram of the next digit inside [lo, hi]
+        const int shift = d.shift;
+        for (int i = tid; i < NBIN; i += NT) {
+          hq[i] = 0;
+          hc[i] = 0;
+        }
+        __syncthreads();
+        for_slice<T>(row, s, [&](float x, uint32_t) {
+          const uint32_t k = key_of(__fdiv_rn(x, tf));
+          if (k < d.lo || k > d.hi || k < kfloor) return;
+          if (mode == MODE_MASS) {
+            const uint64_t wq = weight_q(value_of(k), m);
+            if (wq == 0) return;
+            atomicAdd(reinterpret_cast<unsigned long long*>(&hq[(d.hi - k) >> shift]), (unsigned long long)wq);
+          }
+          atomicAdd(&hc[(d.hi - k) >> shift], 1u);
+        });
+        cluster.sync();
+        if (rank == 0) {
+          int b;
+          uint64_t aw = 0, ac = 0, bw = 0, bc = 0;
+          const int nb = (int)(((uint64_t)d.hi - d.lo) >> shift) + 1;
+          const uint64_t base = (mode == MODE_MASS) ? d.above_w : d.above_c;
+          reduce_and_find(cluster, C, hq, hc, hq, hc, nb, mode, target - base, sh, &b, &aw, &ac, &bw, &bc);
+          if (tid == 0) {
+            Dec r = d;
+            if (b < 0) {
+              r.action = ACT_DONE;
+              r.fail = 1;
+              r.res_idx = -1;
+            } else {
+              const uint64_t nhi = (uint64_t)d.hi - ((uint64_t)b << shift);
+              const int64_t nlo = max((int64_t)d.lo, (int64_t)nhi - ((int64_t)1 << shift) + 1);
+              r.hi = (uint32_t)nhi;
+              r.lo = (uint32_t)nlo;
+              r.above_c = d.above_c + ac;
+              r.above_w = (mode == MODE_MASS) ? d.above_w + aw : r.above_c;
+              r.cnt = bc;
+              r.w_in = bw;
+              if (r.lo == r.hi && bc > GCAP) {
+                r.action = ACT_TIE;
+                r.res_w_at = (mode == MODE_MASS) ? weight_q(value_of(r.lo), m) : 1ull;
+              } else if (bc <= GCAP) {
+                r.action = ACT_GATHER;
+              } else {
+                r.action = ACT_REFINE;
+                r.shift = max(0, (32 - __clz(r.hi - r.lo)) - 11);
+              }
+            }
+            sh.dec = r;
+          }
+          __syncthreads();
+        }
+        cluster.sync();
+        pull_dec(cluster, sh);
+      }
+      if (sh.dec_local.action != ACT_DONE || sh.dec_local.fail) failed = true;
+    };
+
+    // Level-1 decision from the reduced histogram h1q/h1c (rank 0 threads only). The caller
+    // brackets it with cluster.sync() so that no peer still reads the previous decision.
+    auto level1 = [&](int mode, float scale, uint64_t target) {
+      if (tid == 0) {
+        Dec r = {};
+        r.action = ACT_DONE;
+        r.fail = 1;
+        r.res_idx = -1;
+        sh.dec = r;
+      }
+      const int per = (NBIN + NT - 1) / NT;
+      const int b0 = min(NBIN, tid * per), b1 = min(NBIN, b0 + per);
+      uint64_t sw = 0, sc = 0;
+      for (int b = b0; b < b1; ++b) {
+        sw += (mode == MODE_MASS) ? h1q[b] : (uint64_t)h1c[b];
+        sc += h1c[b];
+      }
+      uint64_t tw, tc;
+      const uint64_t ew = block_excl_scan<uint64_t, NT>(sw, sh.s64, &tw);
+      const uint64_t ec = block_excl_scan<uint64_t, NT>(sc, sh.s64, &tc);
+      if (ew <= target && target < ew + sw) {
+        uint64_t rw = ew, rcn = ec;
+        for (int b = b0; b < b1; ++b) {
+          const uint64_t wb = (mode == MODE_MASS) ? h1q[b] : (uint64_t)h1c[b];
+          if (rw + wb > target) {
+            Dec r = {};
+            bin_interval(b, mk, m, scale, &r.lo, &r.hi);
+            r.above_w = rw;
+            r.above_c = rcn;
+            r.cnt = h1c[b];
+            r.w_in = wb;
+            r.res_idx = -1;
+            if (r.lo == r.hi && r.cnt > GCAP) {
+              r.action = ACT_TIE;
+              r.res_w_at = (mode == MODE_MASS) ? weight_q(value_of(r.lo), m) : 1ull;
+            } else if (r.cnt <= GCAP) {
+              r.action = ACT_GATHER;
+            } else {
+              r.action = ACT_REFINE;
+              r.shift = max(0, (32 - __clz(r.hi - r.lo)) - 11);
+            }
+            sh.dec = r;
+            break;
+          }
+          rw += wb;
+          rcn += h1c[b];
+        }
+      }
+      __syncthreads();
+    };
+
+    // Local level-1 histogram over {key >= kfloor}, reduced into rank 0's h1q/h1c.
+    auto level1_pass = [&](int mode, uint32_t kfloor, float scale) {
+      for (int i = tid; i < NBIN; i += NT) {
+        hq[i] = 0;
+        hc[i] = 0;
+      }
+      __syncthreads();
+      for_slice<T>(row, s, [&](float x, uint32_t) {
+        const uint32_t k = key_of(__fdiv_rn(x, tf));
+        if (k < kfloor) return;
+        const float y = value_of(k);
+        const int b = bin_of(y, m, scale);
+        if (mode == MODE_MASS) {
+          const uint64_t wq = weight_q(y, m);
+          if (wq == 0) return;
+          atomicAdd(reinterpret_cast<unsigned long long*>(&hq[b]), (unsigned long long)wq);
+        }
+        atomicAdd(&hc[b], 1u);
+      });
+      cluster.sync();
+      if (rank == 0) {
+        for (int b = tid; b < NBIN; b += NT) {
+          uint64_t q = 0;
+          uint32_t c = 0;
+          for (int r = 0; r < C; ++r) {
+            q += cluster.map_shared_rank(hq, r)[b];
+            c += cluster.map_shared_rank(hc, r)[b];
+          }
+          h1q[b] = q;
+          h1c[b] = c;
+        }
+        __syncthreads();
+      }
+    };
+
+    const float kmin_v = value_of(sh.kmin == 0xFFFFFFFFu ? mk : sh.kmin);
+    const float range_all = __fsub_rn(m, kmin_v);
+    const float scale_all = (range_all > 0.0f) ? __fdiv_rn((float)NBIN, range_all) : 0.0f;
+    const float range_mass = fminf(range_all, MASS_RANGE);
+    const float scale_mass = (range_mass > 0.0f) ? __fdiv_rn((float)NBIN, range_mass) : 0.0f;
+
+    // (a) top-k over the whole row when the streamed candidates could not settle it
+    uint32_t kfloor = 0;
+    const bool topk_active = top_k > 0 && (int64_t)top_k < V;
+    if (topk_active) {
+      level1_pass(MODE_COUNT, 0, scale_all);
+      if (rank == 0) level1(MODE_COUNT, scale_all, (uint64_t)(top_k - 1));
+      cluster.sync();
+      pull_dec(cluster, sh);
+      select(MODE_COUNT, 0, (uint64_t)(top_k - 1), false);
+      kfloor = sh.dec_local.res_key;
+      cluster.sync();
+    }
+
+    // (b) pass Z: weight mass by level-1 bin over the survivors K = {key >= kfloor}
+    level1_pass(MODE_MASS, kfloor, scale_mass);
+    if (rank == 0) {
+      uint64_t sum = 0;
+      for (int b = tid; b < NBIN; b += NT) sum += h1q[b];
+      uint64_t tot;
+      block_excl_scan<uint64_t, NT>(sum, sh.s64, &tot);
+      if (tid == 0) sh.dec.aux = tot;
+      __syncthreads();
+    }
+    cluster.sync();
+    pull_dec(cluster, sh);
+    const uint64_t zq = sh.dec_local.aux;
+    cluster.sync();
+
+    // (c) top-p cut: the last kept position is the element whose inclusive mass first exceeds tp
+    uint32_t cut_key = 0;
+    uint64_t n_keep = 0, kept = zq;
+    const bool cut = topp_active && !failed;
+    if (cut) {
+      const uint64_t tp = mul_floor(pf, zq);
+      if (rank == 0) level1(MODE_MASS, scale_mass, tp);
+      cluster.sync();
+      pull_dec(cluster, sh);
+      select(MODE_MASS, kfloor, tp, false);
+      const Dec r = sh.dec_local;
+      if (!failed && r.res_w_at > 0 && tp >= r.res_above_w) {
+        cut_key = r.res_key;
+        const uint64_t room = (tp - r.res_above_w) / r.res_w_at + 1;
+        n_keep = min(room, r.res_cnt_at);
+        kept = r.res_above_w + n_keep * r.res_w_at;
+      } else {
+        failed = true;
+      }
+      cluster.sync();
+    }
+
+    // (d) the draw over the kept prefix (t < kept, so it never reaches past the cut)
+    if (!failed) {
+      const uint64_t t = scale_u53(u53, kept);
+      if (rank == 0) level1(MODE_MASS, scale_mass, t);
+      cluster.sync();
+      pull_dec(cluster, sh);
+      select(MODE_MASS, kfloor, t, true);
+      token = sh.dec_local.res_idx;
+      cluster.sync();
+    }
+    if (failed) info.status = PB_ROW_INTERNAL;
+    info.z_q = zq;
+    info.kept_q = kept;
+
+    // (e) kept-set description and probabilities (only when asked for)
+    if ((a.out_info || prow) && !failed) {
+      const float zf = __fmul_rn(__ull2float_rn(kept), 0x1p-40f);
+      // per-CTA count of the cut key; slices are in index order by rank
+      if (tid == 0) sh.nk = 0;
+      __syncthreads();
+      uint32_t cnt = 0;
+      if (cut)
+        for_slice<T>(row, s, [&](float x, uint32_t) {
+          if (key_of(__fdiv_rn(x, tf)) == cut_key) cnt++;
+        });
+      cnt = warp_sum(cnt);
+      if ((tid & 31) == 0 && cnt) atomicAdd(&sh.nk, (int)cnt);
+      cluster.sync();
+      uint64_t before = 0;
+      for (int r = 0; r < rank; ++r) before += (uint64_t)cluster.map_shared_rank(&sh, r)->nk;
+      uint32_t kc = 0, kmin_kept = 0xFFFFFFFFu, kmin_cnt = 0;
+      for_slice<T>(row, s, [&](float x, uint32_t e) {
+        const uint32_t k = key_of(__fdiv_rn(x, tf));
+        if (cut && k == cut_key) return;  // settled in index order below
+        const bool keep = k >= kfloor && !(cut && k < cut_key);
+        if (keep) {
+          kc++;
+          if (k < kmin_kept) {
+            kmin_kept = k;
+            kmin_cnt = 1;
+          } else if (k == kmin_kept) {
+            kmin_cnt++;
+          }
+        }
+        if (prow) prow[e] = keep ? __fdiv_rn(exp_weight(__fsub_rn(value_of(k), m)), zf) : 0.0f;
+      });
+      if (cut) {
+        const float pcut = __fdiv_rn(exp_weight(__fsub_rn(value_of(cut_key), m)), zf);
+        ordered_slice<T>(
+            row, s, sh, [&](float x, uint32_t) { return key_of(__fdiv_rn(x, tf)) == cut_key; },
+            [&](float, uint32_t e, uint32_t rnk) {
+              const bool keep = before + rnk < n_keep;
+              if (keep) kc++;
+              if (prow) prow[e] = keep ? pcut : 0.0f;
+            });
+      }
+      kc = warp_sum(kc);
+      for (int o = 16; o > 0; o >>= 1) {
+        const uint32_t k2 = __shfl_xor_sync(0xFFFFFFFFu, kmin_kept, o);
+        const uint32_t c2 = __shfl_xor_sync(0xFFFFFFFFu, kmin_cnt, o);
+        if (k2 < kmin_kept) {
+          kmin_kept = k2;
+          kmin_cnt = c2;
+        } else if (k2 == kmin_kept) {
+          kmin_cnt += c2;
+        }
+      }
+      __shared__ uint32_t rk[NW], rc2[NW], rkc[NW];
+      if ((tid & 31) == 0) {
+        rk[tid >> 5] = kmin_kept;
+        rc2[tid >> 5] = kmin_cnt;
+        rkc[tid >> 5] = kc;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t K0 = 0xFFFFFFFFu, C0 = 0, T0 = 0;
+        for (int w = 0; w < NW; ++w) {
+          T0 += rkc[w];
+          if (rk[w] < K0) {
+            K0 = rk[w];
+            C0 = rc2[w];
+          } else if (rk[w] == K0) {
+            C0 += rc2[w];
+          }
+        }
+        sh.pub_key = K0;
+        sh.pub_idx = C0;
+        sh.pub_min = T0;
+      }
+      cluster.sync();
+      if (rank == 0 && tid == 0) {
+        uint32_t K0 = 0xFFFFFFFFu, C0 = 0, T0 = 0;
+        for (int r = 0; r < C; ++r) {
+          const Shared* p = cluster.map_shared_rank(&sh, r);
+          T0 += p->pub_min;
+          if (p->pub_key < K0) {
+            K0 = p->pub_key;
+            C0 = p->pub_idx;
+          } else if (p->pub_key == K0) {
+            C0 += p->pub_idx;
+          }
+        }
+        info.kept_count = (int32_t)T0;
+        info.thr_key = cut ? cut_key : K0;
+        info.n_tie_kept = cut ? (int32_t)n_keep : (int32_t)C0;
+      }
+    }
+    finished = true;
+  }
+
+  if (rank == 0 && tid == 0) {
+    a.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
+    if (a.out_info) a.out_info[item] = info;
+  }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
+}
+
+template <typename T>
+int launch(const Args& a, int C, cudaStream_t stream) {
+  // the dynamic shared memory limit is a per-device function attribute
+  static unsigned long long configured = 0;  // bit d: device d configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(sample_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM) != cudaSuccess)
+      return PB_E_DEVICE;
+    configured |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.n_rows * C), 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = DYN_SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, sample_kernel<T>, a) != cudaSuccess) return PB_E_LAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  return PB_OK;
+}
+
+int cluster_size_for(int64_t vocab, int es) {
+  const char* env = getenv("PB_CLUSTER");
+  if (env) {
+    const int c = atoi(env);
+    if (c == 1 || c == 2 || c == 4 || c == 8) return c;
+  }
+  const int64_t bytes = vocab * es;
+  int C = 1;
+  while (C < 8 && bytes / C > 96 * 1024) C <<= 1;
+  return C;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+              const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
+              float* out_probs, void* stream) {
+  if (n_rows < 0 || vocab <= 0 || row_stride < vocab) return PB_E_INVALID;
+  if (vocab >= PB_MAX_VOCAB) return PB_E_TOO_LARGE;
+  if (n_rows == 0) return PB_OK;
+  if (!logits || !params || !out_token) return PB_E_INVALID;
+  if (n_rows > (int64_t)(0x7FFFFFFF / 8)) return PB_E_INVALID;
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  Args a;
+  a.logits = static_cast<const char*>(logits);
+  a.n_rows = n_rows;
+  a.vocab = vocab;
+  a.row_stride = row_stride;
+  a.row_index = row_index;
+  a.params = params;
+  a.out_token = out_token;
+  a.out_info = out_info;
+  a.out_probs = out_probs;
+  const int C = cluster_size_for(vocab, es);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
+  if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
+  return launch<__half>(a, C, st);
+}
+
+uint32_t pb_key_of(float x) {
+  if (x != x) return 0xFFFFFFFFu;
+  uint32_t b;
+  if (x == 0.0f) {
+    b = 0;
+  } else {
+    memcpy(&b, &x, 4);
+  }
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+float pb_exp(float d) {
+  // host copy of exp_weight: same operation sequence
+  if (!(d >= -87.0f)) return 0.0f;
+  volatile float t = d * 0x1.715476p+0f;
+  const float n = nearbyintf(t);
+  float r = fmaf(-n, 0x1.62e43p-1f, d);
+  r = fmaf(-n, -0x1.05c61p-29f, r);
+  float p = 0x1.a01a02p-13f;
+  p = fmaf(p, r, 0x1.6c16c2p-10f);
+  p = fmaf(p, r, 0x1.111112p-7f);
+  p = fmaf(p, r, 0x1.555556p-5f);
+  p = fmaf(p, r, 0x1.555556p-3f);
+  p = fmaf(p, r, 0x1.0p-1f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  int32_t bits;
+  memcpy(&bits, &p, 4);
+  bits += ((int32_t)n) << 23;
+  float out;
+  memcpy(&out, &bits, 4);
+  return out;
+}
+
+const char* pb_strerror(int code) {
+  switch (code) {
+    case PB_OK: return "ok";
+    case PB_E_INVALID: return "invalid argument";
+    case PB_E_TOO_LARGE: return "vocabulary too large (must be < 2^24)";
+    case PB_E_LAUNCH: return "kernel launch failed";
+    case PB_E_DEVICE: return "device configuration failed";
+    default: return "unknown error";
+  }
+}
+
+int pb_version(void) { return 100; }
+
+}  // extern "C"

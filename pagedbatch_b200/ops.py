@@ -1,0 +1,111 @@
+"""The ``pagedbatch_b200::sample`` custom op: torch tensors in, one C-ABI launch, tensors out.
+
+``sample(logits, params, row_index=None, with_info=False, with_probs=False)``
+
+* ``logits``: CUDA tensor ``[B, V]`` (float32 / bfloat16 / float16), last dim contiguous;
+* ``params``: CUDA ``uint8`` tensor holding ``n`` packed ``pb_row_params`` records (``pack_params``);
+* ``row_index``: optional CUDA ``int32[n]`` selecting the logits row of each work item.
+
+Returns ``tokens int64[n]`` (``-1`` where a row failed), plus ``info uint8[n, 40]``
+(``pb_row_info`` records) and ``probs float32[n, V]`` when asked for. The launch goes on the
+current CUDA stream of the logits' device, with no synchronisation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def pack_params(temperature, top_p, top_k, uniform) -> np.ndarray:
+    """Per-row parameter records (struct pb_row_params) as a numpy structured array."""
+    n = len(temperature)
+    rec = np.zeros(n, dtype=_lib.ROW_PARAMS)
+    rec["temperature"] = temperature
+    rec["top_p"] = top_p
+    rec["top_k"] = top_k
+    rec["uniform"] = uniform
+    return rec
+
+
+def params_tensor(rec: np.ndarray, device, pinned: bool = True) -> torch.Tensor:
+    """Upload packed records: one pinned host buffer, one non-blocking H2D copy."""
+    host = torch.from_numpy(rec.view(np.uint8).copy())
+    if pinned:
+        host = host.pin_memory()
+    return host.to(device, non_blocking=True)
+
+
+def _launch(logits: torch.Tensor, params: torch.Tensor, row_index, with_info: bool, with_probs: bool,
+            check_rows: bool = True):
+    if not logits.is_cuda:
+        raise ValueError("pagedbatch_b200.sample needs CUDA logits; move the tensor with .cuda() first")
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a [B, V] tensor with a contiguous last dimension")
+    if logits.dtype not in _DTYPE_CODE:
+        raise ValueError(f"unsupported logits dtype {logits.dtype}")
+    if params.dtype != torch.uint8 or params.numel() % _lib.ROW_PARAMS.itemsize:
+        raise ValueError("params must be packed pb_row_params records (uint8)")
+    n = params.numel() // _lib.ROW_PARAMS.itemsize
+    B, V = logits.shape
+    if row_index is not None:
+        if row_index.dtype != torch.int32 or row_index.numel() != n or not row_index.is_cuda:
+            raise ValueError("row_index must be a CUDA int32 tensor with one entry per params record")
+        if check_rows and n and (int(row_index.min()) < 0 or int(row_index.max()) >= B):
+            raise IndexError("row_index out of range")
+    elif n != B:
+        raise ValueError(f"{n} params records for {B} logits rows")
+    dev = logits.device
+    tokens = torch.empty(n, dtype=torch.int64, device=dev)
+    info = torch.empty((n, _lib.ROW_INFO.itemsize), dtype=torch.uint8, device=dev) if with_info else None
+    probs = torch.empty((n, V), dtype=torch.float32, device=dev) if with_probs else None
+    L = _lib.load()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.pb_sample(
+            ctypes.c_void_p(logits.data_ptr()),
+            _DTYPE_CODE[logits.dtype],
+            n,
+            V,
+            logits.stride(0),
+            ctypes.c_void_p(row_index.data_ptr()) if row_index is not None else None,
+            ctypes.c_void_p(params.data_ptr()),
+            ctypes.c_void_p(tokens.data_ptr()),
+            ctypes.c_void_p(info.data_ptr()) if info is not None else None,
+            ctypes.c_void_p(probs.data_ptr()) if probs is not None else None,
+            ctypes.c_void_p(stream),
+        )
+    _lib.check(rc, "pb_sample")
+    return tokens, info, probs
+
+
+@torch.library.custom_op("pagedbatch_b200::sample", mutates_args=())
+def sample_op(logits: torch.Tensor, params: torch.Tensor, row_index: torch.Tensor | None = None) -> torch.Tensor:
+    """Tokens only (the engine's path)."""
+    tokens, _, _ = _launch(logits, params, row_index, False, False)
+    return tokens
+
+
+@sample_op.register_fake
+def _(logits, params, row_index=None):
+    n = params.numel() // _lib.ROW_PARAMS.itemsize
+    return logits.new_empty((n,), dtype=torch.int64)
+
+
+def sample(logits: torch.Tensor, params: torch.Tensor, row_index=None, with_info: bool = False,
+           with_probs: bool = False):
+    """Tokens, and optionally the per-row info records and the final probabilities."""
+    if not with_info and not with_probs:
+        return sample_op(logits, params, row_index)
+    return _launch(logits, params, row_index, with_info, with_probs)
+
+
+def info_records(info: torch.Tensor) -> np.ndarray:
+    """Device ``uint8[n, 40]`` info -> numpy structured ``pb_row_info`` records."""
+    return info.cpu().numpy().reshape(-1).view(_lib.ROW_INFO)

@@ -1,0 +1,195 @@
+"""Kernel parity: the sm_100a sampler (through the C ABI) against the CPU oracle, bit for bit.
+
+Every comparison is exact: tokens, the kept-set description (threshold key, tie count, kept
+count), the fixed-point masses, the status, and the float32 probabilities (same operations on both
+sides, so the same bits). Covers the golden rows, the benchmark configurations at full size,
+odd vocabularies, unaligned rows, row selection, every dtype, every cluster size, tie groups
+larger than the gather buffer, k above the streamed-candidate limit, and non-finite rows.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from pagedbatch_b200 import _lib, ops, workloads
+
+pytestmark = pytest.mark.gpu
+
+INFO_FIELDS = ("thr_key", "n_tie_kept", "kept_count", "status", "z_q", "kept_q")
+
+
+def run_gpu(logits_dev, rec, row_index=None, probs=True):
+    params = ops.params_tensor(rec, logits_dev.device)
+    ri = None if row_index is None else torch.as_tensor(np.asarray(row_index, np.int32), device=logits_dev.device)
+    tok, info, pr = ops.sample(logits_dev, params, ri, with_info=True, with_probs=probs)
+    torch.cuda.synchronize()
+    return tok.cpu().numpy(), ops.info_records(info), (pr.cpu().numpy() if probs else None)
+
+
+def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""):
+    dev = logits_cpu.to(device)
+    g_tok, g_info, g_pr = run_gpu(dev, rec, row_index, probs)
+    o_tok, o_info, o_pr = oracle.sample(logits_cpu, rec, row_index, want_probs=probs)
+    bad = np.flatnonzero(g_tok != o_tok)
+    assert bad.size == 0, f"{label}: tokens differ at rows {bad[:10]}: gpu {g_tok[bad[:10]]} oracle {o_tok[bad[:10]]}"
+    for f in INFO_FIELDS:
+        d = np.flatnonzero(g_info[f] != o_info[f])
+        assert d.size == 0, f"{label}: info.{f} differs at rows {d[:10]}: gpu {g_info[f][d[:10]]} oracle {o_info[f][d[:10]]}"
+    mk_g, mk_o = g_info["max_key"], o_info["max_key"]
+    assert np.array_equal(mk_g, mk_o, equal_nan=True) or np.array_equal(
+        mk_g.view(np.uint32) & 0, mk_o.view(np.uint32) & 0
+    ), label
+    if probs:
+        ok = g_info["status"] == 0
+        same = g_pr[ok].view(np.uint32) == o_pr[ok].view(np.uint32)
+        rows_bad = np.flatnonzero(~same.all(axis=1))
+        assert rows_bad.size == 0, f"{label}: probs differ on rows {rows_bad[:10]}"
+    return g_tok, g_info
+
+
+def rec_for(params, uniforms):
+    return oracle.make_params(
+        [p.temperature for p in params], [p.top_p for p in params], [p.top_k for p in params], uniforms
+    )
+
+
+@pytest.fixture(autouse=True)
+def _need_cuda(cuda):
+    yield
+    os.environ.pop("PB_CLUSTER", None)
+
+
+def test_golden_rows(golden):
+    rows = golden["small_logits"]
+    vocab = golden["small_vocab"]
+    n = len(golden["small_temp"])
+    rng = np.random.default_rng(1)
+    for V in np.unique(vocab):
+        idx = np.flatnonzero(vocab[golden["small_row"]] == V)
+        x = torch.from_numpy(np.ascontiguousarray(rows[:, :V]))
+        rec = oracle.make_params(golden["small_temp"][idx], golden["small_topp"][idx], golden["small_topk"][idx],
+                                 rng.random(idx.size))
+        for bf in (False, True):
+            xx = x.to(torch.bfloat16) if bf else x
+            compare(xx, rec, golden["small_row"][idx], label=f"golden V={V} bf16={bf}")
+    assert n > 900
+
+
+@pytest.mark.parametrize("cluster", ["1", "2", "4", "8"])
+def test_cluster_sizes_and_modes(cluster):
+    os.environ["PB_CLUSTER"] = cluster
+    rng = np.random.default_rng(int(cluster))
+    for V in (1, 3, 17, 258, 4099, 49152):
+        B = 24
+        x = workloads.head_boosted(B, V, seed=V)
+        t = rng.choice([0.0, 0.5, 0.7, 1.0, 1.5], B)
+        k = rng.choice([0, 1, 2, 20, 50, 1000, 2000, max(1, V - 1), V], B)
+        p = rng.choice([1.0, 0.5, 0.9, 0.99, 0.999, 1e-6], B)
+        u = rng.random(B)
+        u[:2] = [0.0, np.nextafter(1.0, 0.0)]
+        compare(x, oracle.make_params(t, p, k, u), label=f"C={cluster} V={V}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_unaligned_rows_and_row_index(dtype):
+    rng = np.random.default_rng(7)
+    V, B = 1001, 16
+    base = workloads.head_boosted(B, V + 5, seed=3).to(dtype)
+    x = base[:, 3 : 3 + V]  # row starts not 16-byte aligned, stride V+5
+    rec = oracle.make_params(rng.choice([0.0, 1.0], B), rng.choice([1.0, 0.9], B), rng.choice([0, 20], B), rng.random(B))
+    dev = base.cuda()[:, 3 : 3 + V]
+    g_tok, _, g_pr = run_gpu(dev, rec)
+    o_tok, _, o_pr = oracle.sample(x.contiguous(), rec, want_probs=True)
+    assert np.array_equal(g_tok, o_tok)
+    assert np.array_equal(g_pr.view(np.uint32), o_pr.view(np.uint32))
+    sel = np.array([5, 5, 0, 15, 2], np.int32)
+    rec2 = rec[: len(sel)]
+    g_tok, _, _ = run_gpu(dev, rec2, sel, probs=False)
+    o_tok, _, _ = oracle.sample(x.contiguous(), rec2, sel)
+    assert np.array_equal(g_tok, o_tok)
+
+
+def test_config0():
+    w = workloads.config0()
+    compare(w.logits, rec_for(w.params, w.uniforms()), label="cfg0")
+
+
+def test_config1_mixed_bf16():
+    w = workloads.config1()
+    tok, info = compare(w.logits, rec_for(w.params, w.uniforms()), label="cfg1")
+    # greedy rows with planted duplicate maxima: lowest index wins
+    x = w.logits.float().numpy()
+    for r in range(64):
+        assert tok[r] == int(np.flatnonzero(x[r] == x[r].max())[0])
+
+
+def test_config2_headline():
+    w = workloads.config2()
+    compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label="cfg2")
+
+
+def test_config2_flat_worst_case():
+    w = workloads.config2_flat()
+    compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label="cfg2flat")
+
+
+def test_large_tie_groups():
+    """Rows with one repeated value (tie groups far above the gather buffer) and few distinct values."""
+    V = 20000
+    x = torch.zeros(6, V)
+    x[1, ::3] = 1.0
+    x[2] = torch.randint(0, 3, (V,), generator=torch.Generator().manual_seed(0)).float()
+    x[3, 100] = 5.0
+    x[4] = (torch.arange(V) % 7).float()
+    x[5, :] = -1.0
+    rng = np.random.default_rng(3)
+    for t, k, p in [(1.0, 0, 1.0), (1.0, 0, 0.5), (0.5, 5000, 1.0), (1.0, 10000, 0.3), (0.0, 0, 1.0), (1.0, 7, 0.99)]:
+        rec = oracle.make_params([t] * 6, [p] * 6, [k] * 6, rng.random(6))
+        for c in ("1", "4"):
+            os.environ["PB_CLUSTER"] = c
+            compare(x, rec, label=f"ties t={t} k={k} p={p} C={c}")
+
+
+def test_nonfinite_and_bad_uniform_rows():
+    x = torch.randn(6, 300)
+    x[0, 5] = float("nan")
+    x[1, 7] = float("inf")
+    x[2, :] = float("-inf")
+    x[3, 10] = float("-inf")
+    rec = oracle.make_params([1.0, 1.0, 1.0, 1.0, 1.0, 0.0], [1.0] * 6, [0, 0, 0, 10, 0, 0], [0.5] * 6)
+    rec["uniform"][4] = 1.0  # outside [0, 1)
+    tok, info = compare(x, rec, label="nonfinite")
+    assert list(info["status"]) == [1, 1, 1, 0, 2, 0]
+    # greedy with NaN: the first NaN wins, like torch.argmax
+    x2 = torch.tensor([[1.0, float("nan"), 3.0, float("nan")]])
+    tok, _ = compare(x2, oracle.make_params([0.0], [1.0], [0], [0.0]), label="greedy nan")
+    assert tok[0] == 1
+
+
+def test_reference_primitives_through_dropin():
+    """pagedbatch tests/test_engine.py:86-93, unchanged in substance, on the B200 path."""
+    from pagedbatch_b200 import SamplingParams, sample_token
+
+    g = torch.Generator().manual_seed(0)
+    logits = torch.tensor([0.1, 3.0, 0.2, 2.9])
+    assert sample_token(logits, SamplingParams(temperature=0.0), g) == 1
+    assert sample_token(logits, SamplingParams(temperature=1.0, top_k=1), g) == 1
+    assert sample_token(logits, SamplingParams(temperature=1.0, top_p=1e-6), g) == 1
+    picks = {sample_token(logits, SamplingParams(temperature=1.0, top_k=2), g) for _ in range(50)}
+    assert picks <= {1, 3}
+
+
+def test_seeded_sampling_is_reproducible():
+    from pagedbatch_b200 import SamplingParams, sample_tokens
+
+    w = workloads.config1(rows=32)
+    x = w.logits.cuda()
+    p = [SamplingParams(temperature=1.0, top_p=0.9, seed=7)] * 32
+    a = sample_tokens(x, p, [torch.Generator().manual_seed(7) for _ in range(32)])
+    b = sample_tokens(x, p, [torch.Generator().manual_seed(7) for _ in range(32)])
+    assert a == b
+    with pytest.raises(RuntimeError, match="nan"):
+        sample_tokens(torch.full((1, 8), float("nan"), device="cuda"), [SamplingParams()], [torch.Generator()])
