@@ -183,6 +183,14 @@ def run_ours(args):
         for i in range(max(3, args.warmup)):
             ops.sample_op(bufs[i % NROT], params)
     stream.synchronize()
+    if args.profile:
+        # profiling mode: a few eager launches for ncu, no timing and no JSON line
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                ops.sample_op(bufs[i % NROT], params)
+        torch.cuda.synchronize(dev)
+        print(f"profile launches done: {args.warmup} warm-up + {args.steps} on {w.name}", flush=True)
+        return
 
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
@@ -286,6 +294,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2", choices=["cfg0", "cfg1", "cfg2", "cfg2flat"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="eager launches only (for ncu), no timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

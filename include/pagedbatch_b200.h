@@ -61,6 +61,8 @@ extern "C" {
 #define PB_ROW_BAD_UNIFORM 2 /* uniform outside [0, 1) */
 #define PB_ROW_TIMEOUT 4     /* a bounded wait on a bulk copy gave up; outputs are not valid */
 #define PB_ROW_INTERNAL 8    /* a selection found no element for its target (an internal error) */
+#define PB_ROW_BAD_PARAMS 16 /* temperature < 0 or NaN, top_p outside (0, 1], or top_k < 0
+                                (values SamplingParams rejects, config.py:146-155) */
 
 /* pb_row_info.flags: which path resolved the row (diagnostic) */
 #define PB_PATH_GREEDY 1

@@ -129,6 +129,14 @@ static void sample_row(const float* x, int64_t V, const pb_row_params* prm, ent_
   memset(&inf, 0, sizeof inf);
   if (probs) memset(probs, 0, (size_t)V * 4);
 
+  /* values SamplingParams rejects (config.py:146-155) */
+  if (!(prm->temperature >= 0.0) || !(prm->top_p > 0.0 && prm->top_p <= 1.0) || prm->top_k < 0) {
+    inf.status = PB_ROW_BAD_PARAMS;
+    *tok = -1;
+    if (info) *info = inf;
+    return;
+  }
+
   if (prm->temperature == 0.0) {                   /* greedy: sampling.py:12-13 */
     uint32_t bk = 0; int64_t bi = 0;
     for (int64_t j = 0; j < V; j++) {

@@ -18,7 +18,7 @@ PB_DTYPE = {"float32": 0, "bfloat16": 1, "float16": 2}
 PB_OK = 0
 ERRORS = {-1: "invalid argument", -2: "vocabulary too large", -3: "kernel launch failed", -4: "device configuration failed"}
 
-ROW_OK, ROW_NONFINITE, ROW_BAD_UNIFORM, ROW_TIMEOUT, ROW_INTERNAL = 0, 1, 2, 4, 8
+ROW_OK, ROW_NONFINITE, ROW_BAD_UNIFORM, ROW_TIMEOUT, ROW_INTERNAL, ROW_BAD_PARAMS = 0, 1, 2, 4, 8, 16
 PATH_GREEDY, PATH_SMALL, PATH_LARGE = 1, 2, 4
 MAX_VOCAB = 1 << 24
 

@@ -39,11 +39,12 @@ namespace {
 constexpr int NT = 256;             // threads per CTA
 constexpr int NW = NT / 32;
 constexpr int CHUNK_ELEMS = 2048;   // elements per staged chunk
-constexpr int NSTAGE = 4;           // chunks in flight per CTA
+constexpr int RING_BYTES = 65536;
+constexpr int MAX_STAGE = 16;
 constexpr int CAND_CAP = 4096;      // candidate entries per CTA
 constexpr int CAND_HI = 2048;       // compaction trigger (CAND_CAP - CHUNK_ELEMS)
 constexpr int KSMALL = 1024;        // largest top_k resolved from the streamed candidates
-constexpr int KCAP = 4096;          // survivors of the small path sorted in rank 0
+constexpr int KCAP = 2048;          // survivors of the small path sorted in rank 0
 constexpr int NBIN = 2048;          // histogram bins of the cooperative selection
 constexpr int GCAP = 4096;          // elements gathered into rank 0 for an exact finish
 constexpr int WAIT_POLLS = 20000;   // bounded mbarrier wait (~seconds) before a row reports a timeout
@@ -52,9 +53,9 @@ constexpr float MASS_RANGE = 27.75f;  // below max - 27.75 the 2^40-scaled weigh
 static_assert(CAND_HI + CHUNK_ELEMS <= CAND_CAP, "a chunk must fit after the trigger level");
 
 // dynamic shared memory regions (bytes)
-constexpr int REGION_A = 32768;  // ring | local histograms | small-path survivors
+constexpr int REGION_A = RING_BYTES;  // ring | local histograms | small-path survivors
 constexpr int REGION_B = 32768;  // candidates | gather list (rank 0)
-constexpr int REGION_C = NBIN * 8 + NBIN * 4;  // reduced level-1 histogram (rank 0)
+constexpr int REGION_C = 0;
 constexpr int DYN_SMEM = REGION_A + REGION_B + REGION_C;
 
 struct Args {
@@ -89,8 +90,15 @@ struct Dec {
 enum : int32_t { ACT_DONE = 0, ACT_GATHER = 1, ACT_REFINE = 2, ACT_TIE = 3 };
 enum : int { MODE_COUNT = 0, MODE_MASS = 1 };
 
+struct alignas(16) Finish {
+  int32_t ok, last, n_tie, pad;
+  int64_t token;
+  uint32_t thr_key, pad2;
+  uint64_t zq, kept;
+};
+
 struct Shared {
-  uint64_t mbar[NSTAGE];
+  uint64_t mbar[MAX_STAGE];
   // row parameters
   double temperature, top_p, uniform;
   int32_t top_k, greedy, filtering, status;
@@ -99,8 +107,12 @@ struct Shared {
   // stage-1 state
   int32_t cand_n, overflow, timeout;
   uint32_t thr;
+  float thr_f;
   // published per-CTA stage-1 results (read by the other CTAs of the cluster)
   uint32_t pub_key, pub_idx, pub_min;
+  float pub_best, pub_max, pub_mnv;
+  float row_best, row_max, row_mnv;
+  uint32_t nan_idx;
   int32_t pub_cand_n, pub_overflow, pub_timeout;
   // cluster-wide row facts (identical in every CTA)
   uint32_t mk, arg, kmin;
@@ -111,6 +123,7 @@ struct Shared {
   // decisions
   Dec dec;        // written by rank 0
   Dec dec_local;  // every CTA's copy of rank 0's dec
+  Finish fin;
   // scratch for scans and reductions
   uint64_t s64[NW + 2];
   uint32_t s32[NW + 2];
@@ -274,22 +287,34 @@ __device__ __forceinline__ void warp_append(bool pass, uint32_t key, uint32_t id
 }
 
 // k-th largest key (1 <= k <= total entries) over up to 8 lists of composites; all threads call.
+// Radix select, 8-bit digits; equal digits in a warp are merged (match_any) before the atomic.
 __device__ uint32_t block_kth_key(uint64_t* const* lists, const int32_t* counts, int nlists, int k, Shared& sh) {
   uint32_t prefix = 0, mask = 0;
   uint32_t kk = (uint32_t)k;
+  const int lane = threadIdx.x & 31;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += NT) sh.hist256[i] = 0;
     __syncthreads();
     for (int l = 0; l < nlists; ++l) {
       const uint64_t* L = lists[l];
-      for (int i = threadIdx.x; i < counts[l]; i += NT) {
-        const uint32_t key = comp_key(L[i]);
-        if ((key & mask) == prefix) atomicAdd(&sh.hist256[(key >> shift) & 255], 1u);
+      const int n = counts[l];
+      for (int i0 = 0; i0 < n; i0 += NT) {
+        const int i = i0 + threadIdx.x;
+        bool v = false;
+        uint32_t d = 0;
+        if (i < n) {
+          const uint32_t key = comp_key(L[i]);
+          if ((key & mask) == prefix) {
+            v = true;
+            d = (key >> shift) & 255;
+          }
+        }
+        const uint32_t grp = __match_any_sync(0xFFFFFFFFu, v ? d : (0x100u + lane));
+        if (v && lane == __ffs(grp) - 1) atomicAdd(&sh.hist256[d], (uint32_t)__popc(grp));
       }
     }
     __syncthreads();
     if (threadIdx.x < 32) {
-      const int lane = threadIdx.x;
       uint32_t c[8], sum = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -379,6 +404,100 @@ __device__ int first_of_key(const uint64_t* a, int n, uint32_t key) {
     else hi = mid;
   }
   return lo;
+}
+
+
+// Resolve a small survivor set in one warp: sort (key desc, index asc), fixed-point weights,
+// inclusive scan, top-p cut and the draw. n <= 64; lanes 0..31 of one warp call.
+__device__ void warp_finish(uint64_t* K, int n, float m, bool topp, float pf, uint64_t u53, Finish* f) {
+  const int lane = threadIdx.x & 31;
+  for (int i = n + lane; i < 64; i += 32) K[i] = 0ull;
+  __syncwarp();
+  for (int k = 2; k <= 64; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int lo = 2 * lane - (lane & (j - 1));
+      const int hi = lo + j;
+      const uint64_t x = K[lo], y = K[hi];
+      const bool desc = (lo & k) == 0;
+      if (desc ? (x < y) : (x > y)) {
+        K[lo] = y;
+        K[hi] = x;
+      }
+      __syncwarp();
+    }
+  }
+  const uint64_t a = K[2 * lane], b = K[2 * lane + 1];
+  const uint64_t qa = (2 * lane < n) ? weight_q(value_of(comp_key(a)), m) : 0ull;
+  const uint64_t qb = (2 * lane + 1 < n) ? weight_q(value_of(comp_key(b)), m) : 0ull;
+  const uint64_t s = qa + qb;
+  const uint64_t incl = warp_incl_scan(s);
+  const uint64_t excl = incl - s;
+  const uint64_t zq = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  // first position whose inclusive prefix exceeds t (t < total)
+  auto find = [&](uint64_t t, uint64_t* at) -> int {
+    const bool here = excl <= t && t < incl;
+    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, here);
+    if (bal == 0) return -1;
+    const int src = __ffs(bal) - 1;
+    const int pos = (excl + qa > t) ? 2 * lane : 2 * lane + 1;
+    const uint64_t inc = (excl + qa > t) ? excl + qa : incl;
+    *at = __shfl_sync(0xFFFFFFFFu, inc, src);
+    return __shfl_sync(0xFFFFFFFFu, pos, src);
+  };
+  int last = n - 1;
+  uint64_t kept = zq;
+  bool ok = n > 0;
+  if (ok && topp) {
+    last = find(mul_floor(pf, zq), &kept);
+    ok = last >= 0;
+  }
+  int pick = -1;
+  if (ok) {
+    uint64_t dummy;
+    pick = find(scale_u53(u53, kept), &dummy);
+    ok = pick >= 0;
+  }
+  if (!ok) {
+    last = 0;
+    pick = 0;
+  }
+  const uint32_t tk = comp_key(K[last]);
+  const int c = ((2 * lane <= last && comp_key(a) == tk) ? 1 : 0) + ((2 * lane + 1 <= last && comp_key(b) == tk) ? 1 : 0);
+  const int n_tie = warp_sum(c);
+  if (lane == 0) {
+    f->ok = ok;
+    f->last = last;
+    f->n_tie = n_tie;
+    f->token = ok ? (int64_t)comp_idx(K[pick]) : -1;
+    f->thr_key = tk;
+    f->zq = zq;
+    f->kept = kept;
+  }
+}
+
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Smallest raw value r with key(r / T) >= key(t / T): raw values at or above it are exactly the
+// ones whose scaled key reaches t's scaled key (division can merge neighbouring raw values).
+// Steps down from t one raw value at a time (at most 64 steps, divisions of ordinary values only);
+// when t is not an ordinary value or the step limit is reached it returns -inf, which keeps every
+// value (still exact, only less selective).
+__device__ float tie_floor(float t, float tf) {
+  const float at = fabsf(t);
+  if (!(at >= 0x1p-100f && at <= 0x1p100f) || !(tf >= 0x1p-60f && tf <= 0x1p60f)) return -INFINITY;
+  const uint32_t target = key_of(__fdiv_rn(t, tf));
+  uint32_t u = key_of(t);
+  for (int i = 0; i < 64; ++i) {
+    const float below = value_of(u - 1);
+    if (!(fabsf(below) >= 0x1p-100f)) return -INFINITY;
+    if (key_of(__fdiv_rn(below, tf)) < target) return value_of(u);
+    --u;
+  }
+  return -INFINITY;
 }
 
 // level-1 bin of a key: distance below the max, scaled; non-increasing in the key
@@ -474,14 +593,15 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
   constexpr int CHUNK_VEC = CHUNK_ELEMS / EPV;
   constexpr int VPT = CHUNK_VEC / NT;  // vectors per thread per chunk
+  constexpr int NSTAGE = RING_BYTES / (CHUNK_ELEMS * ES);
   static_assert(CHUNK_VEC % NT == 0, "chunk must split evenly");
 
   extern __shared__ __align__(128) unsigned char dyn[];
   __shared__ Shared sh;
   unsigned char* regA = dyn;
   uint64_t* candB = reinterpret_cast<uint64_t*>(dyn + REGION_A);
-  uint64_t* h1q = reinterpret_cast<uint64_t*>(dyn + REGION_A + REGION_B);
-  uint32_t* h1c = reinterpret_cast<uint32_t*>(dyn + REGION_A + REGION_B + NBIN * 8);
+  uint64_t* h1q = reinterpret_cast<uint64_t*>(regA + NBIN * 12);
+  uint32_t* h1c = reinterpret_cast<uint32_t*>(regA + NBIN * 20);
   uint64_t* hq = reinterpret_cast<uint64_t*>(regA);
   uint32_t* hc = reinterpret_cast<uint32_t*>(regA + NBIN * 8);
 
@@ -506,8 +626,15 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     sh.overflow = 0;
     sh.timeout = 0;
     sh.thr = 0;
+    sh.thr_f = -INFINITY;
     sh.status = PB_ROW_OK;
-    for (int s = 0; s < NSTAGE; ++s) mbar_init(&sh.mbar[s], 1);
+    // parameters the reference's SamplingParams rejects (config.py:146-155)
+    const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
+    if (bad) {
+      sh.status = PB_ROW_BAD_PARAMS;
+      sh.filtering = 0;
+    }
+    for (int st = 0; st < NSTAGE; ++st) mbar_init(&sh.mbar[st], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -520,24 +647,21 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   const Slice s = make_slice(row, V, rank, C);
 
   // ---------------- stage 1: stream the slice ----------------
-  uint32_t bk = 0, be = 0xFFFFFFFFu, mn = 0xFFFFFFFFu;
-  auto visit = [&](float x, uint32_t e, bool& pass) {
-    const float y = greedy ? x : __fdiv_rn(x, tf);
-    const uint32_t k = key_of(y);
-    if (k > bk || (k == bk && e < be)) {
-      bk = k;
-      be = e;
-    }
-    if (k > KEY_NEG_INF && k < mn) mn = k;
-    pass = filtering && k >= sh.thr;
-    return k;
-  };
+  // Raw values are compared directly (x / T is monotone in x for T > 0): a NaN-propagating max,
+  // the first (lowest-index) maximum, the smallest value above -inf for rows that need it, and for
+  // small top-k rows a candidate list of raw values >= a running threshold.
+  const bool track_min = !greedy && !filtering;  // rows that take the cooperative path
+  float runmax = -INFINITY, bestv = -INFINITY, mnv = INFINITY;
+  uint32_t bidx = 0xFFFFFFFFu;
   auto compact = [&](int kth_rank) {
-    // keep the candidates whose key is >= the kth_rank-th largest
+    // keep the candidates whose raw value reaches the kth_rank-th largest (tie-guarded)
     int32_t n = min(sh.cand_n, CAND_CAP);
     uint64_t* lists[1] = {candB};
     int32_t counts[1] = {n};
-    const uint32_t kth = block_kth_key(lists, counts, 1, kth_rank, sh);
+    const uint32_t kth_raw = block_kth_key(lists, counts, 1, kth_rank, sh);
+    if (tid == 0) sh.thr_f = tie_floor(value_of(kth_raw), tf);
+    __syncthreads();
+    const uint32_t kth = key_of(sh.thr_f);
     uint64_t mine[CAND_CAP / NT];
 #pragma unroll
     for (int j = 0; j < CAND_CAP / NT; ++j) {
@@ -554,19 +678,30 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     }
     __syncthreads();
     if (tid == 0) {
-      sh.thr = kth;
       if (sh.cand_n >= CAND_HI) sh.overflow = 1;  // ties hold the list above the trigger
     }
     __syncthreads();
+  };
+  // one element (head or tail), all 32 lanes call
+  auto visit1 = [&](bool valid, float x, uint32_t e, float t) {
+    if (valid) {
+      runmax = fmax_nan(runmax, x);
+      if (x > bestv) {
+        bestv = x;
+        bidx = e;
+      }
+      if (track_min && x > -INFINITY) mnv = fminf(mnv, x);
+    }
+    if (filtering) warp_append(valid && x >= t, key_of(x), e, candB, &sh.cand_n, CAND_CAP);
   };
 
   // scalar head (rank 0): one element per thread, warp-uniform control flow
   for (int64_t t0 = 0; t0 < s.head_n; t0 += NT) {
     const int64_t e = t0 + tid;
-    bool pass = false;
-    uint32_t k = 0;
-    if (e < s.head_n) k = visit(Elem<T>::ld(row + e), (uint32_t)e, pass);
-    if (filtering) warp_append(pass, k, (uint32_t)e, candB, &sh.cand_n, CAND_CAP);
+    const bool valid = e < s.head_n;
+    float x = -INFINITY;
+    if (valid) x = Elem<T>::ld(row + e);
+    visit1(valid, x, (uint32_t)e, sh.thr_f);
   }
   {
     const int64_t nchunks = (s.nvec + CHUNK_VEC - 1) / CHUNK_VEC;
@@ -589,19 +724,45 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       if (sh.timeout) break;
       const int64_t nv = min((int64_t)CHUNK_VEC, s.nvec - c * CHUNK_VEC);
       const uint4* buf = ring + stage * CHUNK_VEC;
+      const float t = sh.thr_f;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * NT + tid;
-        float x[EPV];
         const bool valid = v < nv;
-        if (valid) Elem<T>::unpack(buf[v], x);
-        const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + v) * EPV);
+        float x[EPV];
+        if (valid) {
+          Elem<T>::unpack(buf[v], x);
+        } else {
 #pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          bool pass = false;
-          uint32_t k = 0;
-          if (valid) k = visit(x[q], e0 + q, pass);
-          if (filtering) warp_append(pass, k, e0 + q, candB, &sh.cand_n, CAND_CAP);
+          for (int q = 0; q < EPV; ++q) x[q] = -INFINITY;
+        }
+        const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + v) * EPV);
+        float vm = x[0];
+#pragma unroll
+        for (int q = 1; q < EPV; ++q) vm = fmax_nan(vm, x[q]);
+        runmax = fmax_nan(runmax, vm);
+        if (vm > bestv) {
+          bestv = vm;
+          int jj = EPV - 1;
+#pragma unroll
+          for (int q = EPV - 1; q >= 0; --q)
+            if (x[q] == vm) jj = q;
+          bidx = e0 + jj;
+        }
+        if (track_min) {
+#pragma unroll
+          for (int q = 0; q < EPV; ++q)
+            if (x[q] > -INFINITY) mnv = fminf(mnv, x[q]);
+        }
+        if (filtering) {
+          bool any = false;
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) any |= valid && (x[q] >= t);
+          if (__any_sync(0xFFFFFFFFu, any)) {
+#pragma unroll
+            for (int q = 0; q < EPV; ++q)
+              warp_append(valid && (x[q] >= t), key_of(x[q]), e0 + q, candB, &sh.cand_n, CAND_CAP);
+          }
         }
       }
       __syncthreads();
@@ -618,11 +779,9 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     if (sh.timeout) {
       // let every issued copy land before the shared memory is reused
       if (tid == 0) {
-        const int64_t issued = nchunks;
         for (int st = 0; st < NSTAGE; ++st) {
-          // last chunk issued on this stage, if any
           int64_t last = -1;
-          for (int64_t c = st; c < issued; c += NSTAGE) last = c;
+          for (int64_t c = st; c < nchunks; c += NSTAGE) last = c;
           if (last >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((last / NSTAGE) & 1), WAIT_POLLS);
         }
       }
@@ -631,50 +790,50 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   }
   for (int64_t t0 = 0; t0 < s.tail_n; t0 += NT) {
     const int64_t e = s.tail_e0 + t0 + tid;
-    bool pass = false;
-    uint32_t k = 0;
-    if (t0 + tid < s.tail_n) k = visit(Elem<T>::ld(row + e), (uint32_t)e, pass);
-    if (filtering) warp_append(pass, k, (uint32_t)e, candB, &sh.cand_n, CAND_CAP);
+    const bool valid = t0 + tid < s.tail_n;
+    float x = -INFINITY;
+    if (valid) x = Elem<T>::ld(row + e);
+    visit1(valid, x, (uint32_t)e, sh.thr_f);
   }
   __syncthreads();
   if (filtering && !sh.overflow && sh.cand_n > CAND_CAP) sh.overflow = 1;
   __syncthreads();
   if (filtering && !sh.overflow && sh.cand_n > top_k) compact(top_k);
 
-  // CTA reduction of (max key, lowest index) and min key
+  // CTA reduction: (first maximum, its index), NaN-propagating max, smallest value above -inf
   {
     for (int o = 16; o > 0; o >>= 1) {
-      const uint32_t k2 = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
-      const uint32_t e2 = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-      const uint32_t m2 = __shfl_xor_sync(0xFFFFFFFFu, mn, o);
-      if (k2 > bk || (k2 == bk && e2 < be)) {
-        bk = k2;
-        be = e2;
+      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bestv, o);
+      const uint32_t i2 = __shfl_xor_sync(0xFFFFFFFFu, bidx, o);
+      if (v2 > bestv || (v2 == bestv && i2 < bidx)) {
+        bestv = v2;
+        bidx = i2;
       }
-      mn = min(mn, m2);
+      runmax = fmax_nan(runmax, __shfl_xor_sync(0xFFFFFFFFu, runmax, o));
+      mnv = fminf(mnv, __shfl_xor_sync(0xFFFFFFFFu, mnv, o));
     }
-    __shared__ uint32_t wk[NW], we[NW], wm[NW];
+    __shared__ float wf[NW], wmx[NW], wmn[NW];
+    __shared__ uint32_t wi[NW];
     if ((tid & 31) == 0) {
-      wk[tid >> 5] = bk;
-      we[tid >> 5] = be;
-      wm[tid >> 5] = mn;
+      wf[tid >> 5] = bestv;
+      wi[tid >> 5] = bidx;
+      wmx[tid >> 5] = runmax;
+      wmn[tid >> 5] = mnv;
     }
     __syncthreads();
     if (tid == 0) {
       for (int w = 1; w < NW; ++w) {
-        if (wk[w] > bk || (wk[w] == bk && we[w] < be)) {
-          bk = wk[w];
-          be = we[w];
+        if (wf[w] > bestv || (wf[w] == bestv && wi[w] < bidx)) {
+          bestv = wf[w];
+          bidx = wi[w];
         }
-        mn = min(mn, wm[w]);
+        runmax = fmax_nan(runmax, wmx[w]);
+        mnv = fminf(mnv, wmn[w]);
       }
-      if (s.e_hi <= s.e_lo) {  // empty slice: neutral values
-        bk = 0;
-        be = 0xFFFFFFFFu;
-      }
-      sh.pub_key = bk;
-      sh.pub_idx = be;
-      sh.pub_min = mn;
+      sh.pub_best = bestv;
+      sh.pub_max = runmax;
+      sh.pub_idx = bidx;
+      sh.pub_mnv = mnv;
       sh.pub_cand_n = min(sh.cand_n, CAND_CAP);
       sh.pub_overflow = sh.overflow;
       sh.pub_timeout = sh.timeout;
@@ -683,32 +842,35 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   cluster.sync();  // S1: stage-1 results visible cluster-wide
 
   if (tid == 0) {
-    uint32_t mk = 0, arg = 0xFFFFFFFFu, kmin = 0xFFFFFFFFu;
+    float bv = -INFINITY, rm = -INFINITY, mn = INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
     int ov = 0, to = 0;
     for (int r = 0; r < C; ++r) {
       const Shared* p = cluster.map_shared_rank(&sh, r);
-      const uint32_t k = p->pub_key, e = p->pub_idx;
-      if (k > mk || (k == mk && e < arg)) {
-        mk = k;
-        arg = e;
+      if (p->pub_best > bv || (p->pub_best == bv && p->pub_idx < bi)) {
+        bv = p->pub_best;
+        bi = p->pub_idx;
       }
-      kmin = min(kmin, p->pub_min);
+      rm = fmax_nan(rm, p->pub_max);
+      mn = fminf(mn, p->pub_mnv);
       ov |= p->pub_overflow;
       to |= p->pub_timeout;
     }
-    sh.mk = mk;
-    sh.arg = arg;
-    sh.kmin = kmin;
+    sh.row_best = bv;
+    sh.row_max = rm;
+    sh.row_mnv = mn;
+    sh.arg = (bi == 0xFFFFFFFFu) ? 0u : bi;  // every value -inf: the first index
     sh.any_overflow = ov;
     sh.any_timeout = to;
   }
   __syncthreads();
 
-  const uint32_t mk = sh.mk;
-  const float m = value_of(mk);
+  // scaled extremes: x / T is monotone, so the extreme raw values give the extreme keys
+  const float m = greedy ? sh.row_max : __fdiv_rn(sh.row_max, tf);
+  const uint32_t mk = key_of(m);
   float* prow = a.out_probs ? a.out_probs + item * V : nullptr;
   pb_row_info info = {};
-  info.max_key = greedy ? value_of(mk) : m;
+  info.max_key = (greedy && sh.row_max == sh.row_max) ? sh.row_best : m;
   int64_t token = -1;
   bool finished = false;
 
@@ -720,9 +882,29 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   if (sh.any_timeout) {
     info.status = PB_ROW_TIMEOUT;
     finished = true;
+  } else if (sh.status != PB_ROW_OK) {
+    info.status = sh.status;
+    info.max_key = 0.0f;
+    finished = true;
   } else if (greedy) {
+    if (sh.row_max != sh.row_max) {
+      // NaN in the row: torch.argmax returns the first NaN
+      if (tid == 0) sh.nan_idx = 0xFFFFFFFFu;
+      __syncthreads();
+      for_slice<T>(row, s, [&](float x, uint32_t e) {
+        if (x != x) atomicMin(&sh.nan_idx, e);
+      });
+      __syncthreads();
+      cluster.sync();
+      if (tid == 0) {
+        uint32_t ni = 0xFFFFFFFFu;
+        for (int r = 0; r < C; ++r) ni = min(ni, cluster.map_shared_rank(&sh, r)->nan_idx);
+        sh.arg = ni;
+      }
+      __syncthreads();
+    }
     token = sh.arg;
-    info.thr_key = mk;
+    info.thr_key = key_of(info.max_key);
     info.n_tie_kept = 1;
     info.kept_count = 1;
     info.flags = PB_PATH_GREEDY;
@@ -744,7 +926,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
 
   // ---------------- small path: survivors resolved in rank 0 ----------------
   if (!finished && filtering && !sh.any_overflow) {
-    uint64_t* K = reinterpret_cast<uint64_t*>(regA);
+    uint64_t* K = reinterpret_cast<uint64_t*>(regA + NBIN * 24);
     zero_probs();
     if (rank == 0) {
       uint64_t* lists[8];
@@ -755,7 +937,8 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         counts[r] = cluster.map_shared_rank(&sh, r)->pub_cand_n;
         total += counts[r];
       }
-      const uint32_t kth = block_kth_key(lists, counts, C, min(top_k, total), sh);
+      const uint32_t kth_raw = block_kth_key(lists, counts, C, min(top_k, total), sh);
+      const uint32_t kth = key_of(__fdiv_rn(value_of(kth_raw), tf));
       if (tid == 0) sh.nk = 0;
       __syncthreads();
       for (int r = 0; r < C; ++r) {
@@ -763,13 +946,34 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         for (int i0 = 0; i0 < counts[r]; i0 += NT) {
           const int i = i0 + tid;
           const uint64_t c = (i < counts[r]) ? L[i] : 0ull;
-          const bool keep = c != 0ull && comp_key(c) >= kth;
-          warp_append(keep, comp_key(c), comp_idx(c), K, &sh.nk, KCAP);
+          const uint32_t k = (c != 0ull) ? key_of(__fdiv_rn(value_of(comp_key(c)), tf)) : 0u;
+          warp_append(c != 0ull && k >= kth, k, comp_idx(c), K, &sh.nk, KCAP);
         }
       }
       __syncthreads();
       const int nk = sh.nk;
-      if (nk <= KCAP) {
+      if (nk <= 64) {
+        Finish f;
+        if (tid < 32) warp_finish(K, nk, m, topp_active, pf, u53, &f);
+        if (tid == 0) sh.fin = f;
+        __syncthreads();
+        f = sh.fin;
+        if (tid == 0) {
+          if (!f.ok) info.status = PB_ROW_INTERNAL;
+          token = f.token;
+          info.thr_key = f.thr_key;
+          info.n_tie_kept = f.n_tie;
+          info.kept_count = f.last + 1;
+          info.z_q = f.zq;
+          info.kept_q = f.kept;
+          info.flags = PB_PATH_SMALL;
+          sh.nk = nk;
+          sh.found_pos = f.last;
+          sh.s64[NW + 1] = f.kept;
+          sh.dec.action = ACT_DONE;
+        }
+        __syncthreads();
+      } else if (nk <= KCAP) {
         block_sort_desc(K, nk);
         uint64_t zq;
         {
@@ -1092,7 +1296,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       }
     };
 
-    const float kmin_v = value_of(sh.kmin == 0xFFFFFFFFu ? mk : sh.kmin);
+    const float kmin_v = (sh.row_mnv < INFINITY) ? __fdiv_rn(sh.row_mnv, tf) : m;
     const float range_all = __fsub_rn(m, kmin_v);
     const float scale_all = (range_all > 0.0f) ? __fdiv_rn((float)NBIN, range_all) : 0.0f;
     const float range_mass = fminf(range_all, MASS_RANGE);
@@ -1260,7 +1464,17 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
 
   if (rank == 0 && tid == 0) {
     a.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
-    if (a.out_info) a.out_info[item] = info;
+    if (a.out_info) {  // field by field: records sit at 40-byte strides
+      pb_row_info* o = a.out_info + item;
+      o->thr_key = info.thr_key;
+      o->n_tie_kept = info.n_tie_kept;
+      o->kept_count = info.kept_count;
+      o->status = info.status;
+      o->max_key = info.max_key;
+      o->flags = info.flags;
+      o->z_q = info.z_q;
+      o->kept_q = info.kept_q;
+    }
   }
   cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
@@ -1293,15 +1507,26 @@ int launch(const Args& a, int C, cudaStream_t stream) {
   return PB_OK;
 }
 
-int cluster_size_for(int64_t vocab, int es) {
+// Cluster size: enough CTAs to fill every SM twice, but slices of at least 16 KB.
+int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
   const char* env = getenv("PB_CLUSTER");
   if (env) {
     const int c = atoi(env);
     if (c == 1 || c == 2 || c == 4 || c == 8) return c;
   }
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  const int64_t want = 2LL * sms[dev];
   const int64_t bytes = vocab * es;
   int C = 1;
-  while (C < 8 && bytes / C > 96 * 1024) C <<= 1;
+  while (C < 8 && n_rows * C < want && bytes / (2 * C) >= 16384) C <<= 1;
   return C;
 }
 
@@ -1330,7 +1555,7 @@ int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int6
   a.out_token = out_token;
   a.out_info = out_info;
   a.out_probs = out_probs;
-  const int C = cluster_size_for(vocab, es);
+  const int C = cluster_size_for(n_rows, vocab, es);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
   if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);

@@ -38,10 +38,7 @@ def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""
     for f in INFO_FIELDS:
         d = np.flatnonzero(g_info[f] != o_info[f])
         assert d.size == 0, f"{label}: info.{f} differs at rows {d[:10]}: gpu {g_info[f][d[:10]]} oracle {o_info[f][d[:10]]}"
-    mk_g, mk_o = g_info["max_key"], o_info["max_key"]
-    assert np.array_equal(mk_g, mk_o, equal_nan=True) or np.array_equal(
-        mk_g.view(np.uint32) & 0, mk_o.view(np.uint32) & 0
-    ), label
+    assert np.array_equal(g_info["max_key"], o_info["max_key"], equal_nan=True), label
     if probs:
         ok = g_info["status"] == 0
         same = g_pr[ok].view(np.uint32) == o_pr[ok].view(np.uint32)
@@ -163,10 +160,20 @@ def test_nonfinite_and_bad_uniform_rows():
     rec["uniform"][4] = 1.0  # outside [0, 1)
     tok, info = compare(x, rec, label="nonfinite")
     assert list(info["status"]) == [1, 1, 1, 0, 2, 0]
-    # greedy with NaN: the first NaN wins, like torch.argmax
-    x2 = torch.tensor([[1.0, float("nan"), 3.0, float("nan")]])
-    tok, _ = compare(x2, oracle.make_params([0.0], [1.0], [0], [0.0]), label="greedy nan")
-    assert tok[0] == 1
+    # greedy with NaN: the first NaN wins, like torch.argmax; an all -inf row picks index 0
+    x2 = torch.tensor([[1.0, float("nan"), 3.0, float("nan")], [float("-inf")] * 4, [-0.0, 0.0, -1.0, 0.0]])
+    tok, _ = compare(x2, oracle.make_params([0.0] * 3, [1.0] * 3, [0] * 3, [0.0] * 3), label="greedy edge")
+    assert list(tok) == [1, 0, 0]
+
+
+def test_rejected_parameters_report_status():
+    x = torch.randn(4, 100)
+    rec = oracle.make_params([-1.0, 1.0, 1.0, float("nan")], [1.0, 0.0, 1.5, 1.0], [0, 0, 0, 0], [0.5] * 4)
+    tok, info = compare(x, rec, label="bad params")
+    assert list(info["status"]) == [16, 16, 16, 16] and list(tok) == [-1] * 4
+    rec = oracle.make_params([1.0], [1.0], [-3], [0.5])
+    tok, info = compare(x[:1], rec, label="bad top_k")
+    assert info["status"][0] == 16
 
 
 def test_reference_primitives_through_dropin():
