@@ -755,13 +755,25 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             if (x[q] > -INFINITY) mnv = fminf(mnv, x[q]);
         }
         if (filtering) {
-          bool any = false;
+          // one warp-aggregated append per vector: scan the lanes' survivor counts, reserve once
+          uint32_t pm = 0;
 #pragma unroll
-          for (int q = 0; q < EPV; ++q) any |= valid && (x[q] >= t);
-          if (__any_sync(0xFFFFFFFFu, any)) {
+          for (int q = 0; q < EPV; ++q)
+            if (valid && x[q] >= t) pm |= 1u << q;
+          const uint32_t cnt = (uint32_t)__popc(pm);
+          if (__any_sync(0xFFFFFFFFu, cnt != 0)) {
+            const uint32_t incl = warp_incl_scan(cnt);
+            uint32_t base = 0;
+            if ((tid & 31) == 31) base = (uint32_t)atomicAdd(&sh.cand_n, (int)incl);
+            base = __shfl_sync(0xFFFFFFFFu, base, 31);
+            uint32_t pos = base + incl - cnt;
 #pragma unroll
-            for (int q = 0; q < EPV; ++q)
-              warp_append(valid && (x[q] >= t), key_of(x[q]), e0 + q, candB, &sh.cand_n, CAND_CAP);
+            for (int q = 0; q < EPV; ++q) {
+              if ((pm >> q) & 1u) {
+                if (pos < (uint32_t)CAND_CAP) candB[pos] = compose(key_of(x[q]), e0 + q);
+                ++pos;
+              }
+            }
           }
         }
       }
@@ -798,7 +810,8 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   __syncthreads();
   if (filtering && !sh.overflow && sh.cand_n > CAND_CAP) sh.overflow = 1;
   __syncthreads();
-  if (filtering && !sh.overflow && sh.cand_n > top_k) compact(top_k);
+  // with more than one CTA per row, shrink each list to its local survivors before the merge
+  if (filtering && C > 1 && !sh.overflow && sh.cand_n > top_k) compact(top_k);
 
   // CTA reduction: (first maximum, its index), NaN-propagating max, smallest value above -inf
   {
@@ -1507,7 +1520,7 @@ int launch(const Args& a, int C, cudaStream_t stream) {
   return PB_OK;
 }
 
-// Cluster size: enough CTAs to fill every SM twice, but slices of at least 16 KB.
+// Cluster size: enough CTAs to give every SM one, but slices of at least 16 KB.
 int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
   const char* env = getenv("PB_CLUSTER");
   if (env) {
@@ -1523,7 +1536,7 @@ int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     sms[dev] = n;
   }
-  const int64_t want = 2LL * sms[dev];
+  const int64_t want = sms[dev];
   const int64_t bytes = vocab * es;
   int C = 1;
   while (C < 8 && n_rows * C < want && bytes / (2 * C) >= 16384) C <<= 1;
