@@ -11,7 +11,7 @@
 //     list of keys >= a running threshold (the k-th largest key seen so far: a lower bound of the
 //     row's k-th key, so no survivor is ever dropped).
 //  2. Greedy rows finish here. Small top-k rows finish in rank 0's shared memory: exact k-th key
-//     by radix select over the candidates of all C CTAs (read through distributed shared memory),
+//     by bisection over the candidates of all C CTAs (copied through distributed shared memory),
 //     the survivors sorted by (key desc, index asc), fixed-point weights scanned for the top-p
 //     cut and the draw.
 //  3. Other rows (temperature-only, top-p over the full vocabulary, large k): the cluster re-reads
@@ -38,11 +38,12 @@ namespace {
 
 constexpr int NT = 256;             // threads per CTA
 constexpr int NW = NT / 32;
-constexpr int CHUNK_ELEMS = 2048;   // elements per staged chunk
+constexpr int CHUNK_BYTES = 16384;  // bytes per staged chunk
 constexpr int RING_BYTES = 65536;
 constexpr int MAX_STAGE = 16;
 constexpr int CAND_CAP = 4096;      // candidate entries per CTA
-constexpr int CAND_HI = 2048;       // compaction trigger (CAND_CAP - CHUNK_ELEMS)
+constexpr int SLOTS = CAND_CAP / NT; // candidate slots per thread
+constexpr uint32_t BUCKET = 32;     // keys left between the bisection bounds when it stops early
 constexpr int KSMALL = 1024;        // largest top_k resolved from the streamed candidates
 constexpr int KCAP = 2048;          // survivors of the small path sorted in rank 0
 constexpr int NBIN = 2048;          // histogram bins of the cooperative selection
@@ -50,7 +51,7 @@ constexpr int GCAP = 4096;          // elements gathered into rank 0 for an exac
 constexpr int WAIT_POLLS = 20000;   // bounded mbarrier wait (~seconds) before a row reports a timeout
 constexpr float MASS_RANGE = 27.75f;  // below max - 27.75 the 2^40-scaled weight is 0
 
-static_assert(CAND_HI + CHUNK_ELEMS <= CAND_CAP, "a chunk must fit after the trigger level");
+static_assert(CAND_CAP % NT == 0, "slots split evenly");
 
 // dynamic shared memory regions (bytes)
 constexpr int REGION_A = RING_BYTES;  // ring | local histograms | small-path survivors
@@ -127,10 +128,11 @@ struct Shared {
   // scratch for scans and reductions
   uint64_t s64[NW + 2];
   uint32_t s32[NW + 2];
-  uint32_t sel_digit, sel_kk;
   int32_t found_pos;
   uint64_t found_incl;
-  uint32_t hist256[256];
+  uint32_t red[5 * NW];  // block reductions (sums, maxima, two bisection buffers, minima)
+  uint32_t bucket_n, bucket_kth;
+  uint32_t bucket[BUCKET];
 };
 
 template <typename T>
@@ -286,63 +288,92 @@ __device__ __forceinline__ void warp_append(bool pass, uint32_t key, uint32_t id
   }
 }
 
-// k-th largest key (1 <= k <= total entries) over up to 8 lists of composites; all threads call.
-// Radix select, 8-bit digits; equal digits in a warp are merged (match_any) before the atomic.
-__device__ uint32_t block_kth_key(uint64_t* const* lists, const int32_t* counts, int nlists, int k, Shared& sh) {
-  uint32_t prefix = 0, mask = 0;
-  uint32_t kk = (uint32_t)k;
-  const int lane = threadIdx.x & 31;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += NT) sh.hist256[i] = 0;
-    __syncthreads();
-    for (int l = 0; l < nlists; ++l) {
-      const uint64_t* L = lists[l];
-      const int n = counts[l];
-      for (int i0 = 0; i0 < n; i0 += NT) {
-        const int i = i0 + threadIdx.x;
-        bool v = false;
-        uint32_t d = 0;
-        if (i < n) {
-          const uint32_t key = comp_key(L[i]);
-          if ((key & mask) == prefix) {
-            v = true;
-            d = (key >> shift) & 255;
-          }
-        }
-        const uint32_t grp = __match_any_sync(0xFFFFFFFFu, v ? d : (0x100u + lane));
-        if (v && lane == __ffs(grp) - 1) atomicAdd(&sh.hist256[d], (uint32_t)__popc(grp));
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      uint32_t c[8], sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = sh.hist256[255 - lane * 8 - j];
-        sum += c[j];
-      }
-      const uint32_t incl = warp_incl_scan(sum);
-      const uint32_t excl = incl - sum;
-      if (excl < kk && kk <= incl) {
-        uint32_t r = excl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (r + c[j] >= kk) {
-            sh.sel_digit = 255 - lane * 8 - j;
-            sh.sel_kk = kk - r;
-            break;
-          }
-          r += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    prefix |= sh.sel_digit << shift;
-    mask |= 0xFFu << shift;
-    kk = sh.sel_kk;
-    __syncthreads();
+// Block-wide (sum, min, max) of one value per thread; every thread gets all three. All threads
+// call; the caller separates two calls (and any later use of sh.red) with a barrier.
+__device__ __forceinline__ void block_sum_min_max(uint32_t v, uint32_t mn, uint32_t mx, Shared& sh, uint32_t* sum_out,
+                                                  uint32_t* min_out, uint32_t* max_out) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = __reduce_add_sync(0xFFFFFFFFu, v);
+  mn = __reduce_min_sync(0xFFFFFFFFu, mn);
+  mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+  if (lane == 0) {
+    sh.red[w] = v;
+    sh.red[NW + w] = mx;
+    sh.red[4 * NW + w] = mn;
   }
-  return prefix;
+  __syncthreads();
+  uint32_t s = 0, lo = 0xFFFFFFFFu, hi = 0;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    s += sh.red[i];
+    hi = max(hi, sh.red[NW + i]);
+    lo = min(lo, sh.red[4 * NW + i]);
+  }
+  *sum_out = s;
+  *min_out = lo;
+  *max_out = hi;
+}
+
+// k-th largest of the keys the block's threads hold in registers (N per thread), by bisection on
+// the key. On entry c_lo = number of held keys >= lo (at least k) and every held key is < hi_excl;
+// held keys below lo (fillers) never count. The bisection stops once at most BUCKET keys lie in
+// [lo, hi). exact = false returns lo (a lower bound: at least k keys are >= lo, and at most BUCKET
+// more than are >= the k-th); exact = true finishes inside the bucket and returns the k-th key
+// itself. Every thread returns the same key. All threads call; the caller puts a barrier between
+// this and the next use of sh.red.
+template <int N>
+__device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint32_t lo, uint32_t c_lo,
+                                     uint64_t hi_excl, bool exact, Shared& sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint64_t hi = hi_excl;
+  uint32_t c_hi = 0;  // held keys >= hi (fewer than k)
+  int par = 0;
+  while (hi - lo > 1 && c_lo - c_hi > BUCKET) {
+    const uint32_t mid = (uint32_t)(lo + ((hi - lo) >> 1));
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < N; ++j) c += (key[j] >= mid) ? 1u : 0u;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    if (lane == 0) sh.red[2 * NW + par * NW + w] = c;
+    __syncthreads();
+    uint32_t tot = 0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) tot += sh.red[2 * NW + par * NW + i];
+    if (tot >= k) {
+      lo = mid;
+      c_lo = tot;
+    } else {
+      hi = mid;
+      c_hi = tot;
+    }
+    par ^= 1;
+  }
+  if (!exact || hi - lo <= 1) return lo;
+  // c_lo - c_hi <= BUCKET keys lie in [lo, hi); the answer is the (k - c_hi)-th largest of them
+  if (threadIdx.x == 0) sh.bucket_n = 0;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    if (key[j] >= lo && (uint64_t)key[j] < hi) {
+      const uint32_t pos = atomicAdd(&sh.bucket_n, 1u);
+      if (pos < BUCKET) sh.bucket[pos] = key[j];
+    }
+  }
+  __syncthreads();
+  if (w == 0) {
+    const uint32_t n = min(sh.bucket_n, BUCKET);
+    const uint32_t mine = (uint32_t)lane < n ? sh.bucket[lane] : 0u;
+    uint32_t gt = 0, ge = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+      const uint32_t b = sh.bucket[i];
+      gt += (b > mine) ? 1u : 0u;
+      ge += (b >= mine) ? 1u : 0u;
+    }
+    const uint32_t r = k - c_hi;
+    if ((uint32_t)lane < n && gt < r && r <= ge) sh.bucket_kth = mine;  // equal keys write the same value
+  }
+  __syncthreads();
+  return sh.bucket_kth;
 }
 
 // Sort up to 4096 composites descending (bitonic network in shared memory); all threads call.
@@ -591,9 +622,10 @@ __device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq,
 template <typename T>
 __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
-  constexpr int CHUNK_VEC = CHUNK_ELEMS / EPV;
+  constexpr int CHUNK_VEC = CHUNK_BYTES / 16;
   constexpr int VPT = CHUNK_VEC / NT;  // vectors per thread per chunk
-  constexpr int NSTAGE = RING_BYTES / (CHUNK_ELEMS * ES);
+  constexpr int NSTAGE = RING_BYTES / CHUNK_BYTES;
+  (void)ES;
   static_assert(CHUNK_VEC % NT == 0, "chunk must split evenly");
 
   extern __shared__ __align__(128) unsigned char dyn[];
@@ -649,60 +681,65 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   // ---------------- stage 1: stream the slice ----------------
   // Raw values are compared directly (x / T is monotone in x for T > 0): a NaN-propagating max,
   // the first (lowest-index) maximum, the smallest value above -inf for rows that need it, and for
-  // small top-k rows a candidate list of raw values >= a running threshold.
+  // small top-k rows the candidates (raw value >= a running threshold) in per-thread slots.
+  // Each thread handles VPT independent 16-byte vectors per 16 KB chunk.
   const bool track_min = !greedy && !filtering;  // rows that take the cooperative path
   float runmax = -INFINITY, bestv = -INFINITY, mnv = INFINITY;
   uint32_t bidx = 0xFFFFFFFFu;
+  int nc = 0;             // this thread's occupied candidate slots
+  bool ovf = false;       // a candidate of this thread found no free slot
+  bool row_ovf = false;   // some thread of the CTA overflowed (uniform: from __syncthreads_or)
+
+  auto push = [&](float x, uint32_t e) {
+    if (nc < SLOTS) {
+      candB[nc * NT + tid] = compose(key_of(x), e);
+      ++nc;
+    } else {
+      ovf = true;
+    }
+  };
+  // Raise the threshold to the tie floor of the kth_rank-th largest candidate and drop the
+  // candidates below it (each thread compacts its own slots). All threads call; a barrier
+  // separates two calls.
   auto compact = [&](int kth_rank) {
-    // keep the candidates whose raw value reaches the kth_rank-th largest (tie-guarded)
-    int32_t n = min(sh.cand_n, CAND_CAP);
-    uint64_t* lists[1] = {candB};
-    int32_t counts[1] = {n};
-    const uint32_t kth_raw = block_kth_key(lists, counts, 1, kth_rank, sh);
+    uint32_t kk[SLOTS];
+    uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+    for (int j = 0; j < SLOTS; ++j) {
+      kk[j] = (j < nc) ? comp_key(candB[j * NT + tid]) : 0u;
+      if (j < nc) mn = min(mn, kk[j]);
+      mx = max(mx, kk[j]);
+    }
+    uint32_t tot, kmin, kmax;
+    block_sum_min_max((uint32_t)nc, mn, mx, sh, &tot, &kmin, &kmax);
+    if ((int)tot < kth_rank) return;  // fewer candidates than k: nothing to raise
+    // a lower bound of the kth_rank-th candidate (at most BUCKET more candidates above it)
+    const uint32_t kth_raw = block_kth_select<SLOTS>(kk, (uint32_t)kth_rank, kmin, tot, (uint64_t)kmax + 1, false, sh);
+    __syncthreads();  // every thread has read the old threshold
     if (tid == 0) sh.thr_f = tie_floor(value_of(kth_raw), tf);
     __syncthreads();
-    const uint32_t kth = key_of(sh.thr_f);
-    uint64_t mine[CAND_CAP / NT];
+    const uint32_t fk = key_of(sh.thr_f);
+    int w = 0;
 #pragma unroll
-    for (int j = 0; j < CAND_CAP / NT; ++j) {
-      const int i = j * NT + tid;
-      mine[j] = (i < n) ? candB[i] : 0ull;
-    }
-    __syncthreads();
-    if (tid == 0) sh.cand_n = 0;
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < CAND_CAP / NT; ++j) {
-      const bool keep = mine[j] != 0ull && comp_key(mine[j]) >= kth;
-      warp_append(keep, comp_key(mine[j]), comp_idx(mine[j]), candB, &sh.cand_n, CAND_CAP);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      if (sh.cand_n >= CAND_HI) sh.overflow = 1;  // ties hold the list above the trigger
-    }
-    __syncthreads();
-  };
-  // one element (head or tail), all 32 lanes call
-  auto visit1 = [&](bool valid, float x, uint32_t e, float t) {
-    if (valid) {
-      runmax = fmax_nan(runmax, x);
-      if (x > bestv) {
-        bestv = x;
-        bidx = e;
+    for (int j = 0; j < SLOTS; ++j) {
+      if (j < nc && kk[j] >= fk) {
+        candB[w * NT + tid] = candB[j * NT + tid];
+        ++w;
       }
-      if (track_min && x > -INFINITY) mnv = fminf(mnv, x);
     }
-    if (filtering) warp_append(valid && x >= t, key_of(x), e, candB, &sh.cand_n, CAND_CAP);
+    nc = w;
+  };
+  auto visit1 = [&](float x, uint32_t e) {
+    runmax = fmax_nan(runmax, x);
+    if (x > bestv) {
+      bestv = x;
+      bidx = e;
+    }
+    if (track_min && x > -INFINITY) mnv = fminf(mnv, x);
   };
 
-  // scalar head (rank 0): one element per thread, warp-uniform control flow
-  for (int64_t t0 = 0; t0 < s.head_n; t0 += NT) {
-    const int64_t e = t0 + tid;
-    const bool valid = e < s.head_n;
-    float x = -INFINITY;
-    if (valid) x = Elem<T>::ld(row + e);
-    visit1(valid, x, (uint32_t)e, sh.thr_f);
-  }
+  // scalar head (rank 0): max only; filtered after the stream against the final threshold
+  for (int64_t e = tid; e < s.head_n; e += NT) visit1(Elem<T>::ld(row + e), (uint32_t)e);
   {
     const int64_t nchunks = (s.nvec + CHUNK_VEC - 1) / CHUNK_VEC;
     const uint4* src = reinterpret_cast<const uint4*>(row + s.vec_e0);
@@ -716,68 +753,92 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         bulk_load(ring + c * CHUNK_VEC, src + (int64_t)c * CHUNK_VEC, (uint32_t)(nv * 16), &sh.mbar[c], pol);
       }
     }
+    bool have_thr = !filtering;
     for (int64_t c = 0; c < nchunks; ++c) {
       const int stage = (int)(c % NSTAGE);
       const uint32_t parity = (uint32_t)((c / NSTAGE) & 1);
       if (!mbar_wait_bounded(&sh.mbar[stage], parity, WAIT_POLLS)) sh.timeout = 1;
       __syncthreads();
       if (sh.timeout) break;
-      const int64_t nv = min((int64_t)CHUNK_VEC, s.nvec - c * CHUNK_VEC);
+      const int nv = (int)min((int64_t)CHUNK_VEC, s.nvec - c * CHUNK_VEC);
       const uint4* buf = ring + stage * CHUNK_VEC;
-      const float t = sh.thr_f;
+      // load every vector of this thread first (independent shared loads), then reduce
+      float x[VPT][EPV];
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * NT + tid;
-        const bool valid = v < nv;
-        float x[EPV];
-        if (valid) {
-          Elem<T>::unpack(buf[v], x);
+        if (v < nv) {
+          Elem<T>::unpack(buf[v], x[j]);
         } else {
 #pragma unroll
-          for (int q = 0; q < EPV; ++q) x[q] = -INFINITY;
+          for (int q = 0; q < EPV; ++q) x[j][q] = -INFINITY;
         }
-        const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + v) * EPV);
-        float vm = x[0];
+      }
+      float vm[VPT];
 #pragma unroll
-        for (int q = 1; q < EPV; ++q) vm = fmax_nan(vm, x[q]);
-        runmax = fmax_nan(runmax, vm);
-        if (vm > bestv) {
-          bestv = vm;
+      for (int j = 0; j < VPT; ++j) {
+        float a = fmax_nan(x[j][0], x[j][1]);
+#pragma unroll
+        for (int q = 2; q < EPV; ++q) a = fmax_nan(a, x[j][q]);
+        vm[j] = a;
+      }
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        runmax = fmax_nan(runmax, vm[j]);
+        if (vm[j] > bestv) {
+          bestv = vm[j];
           int jj = EPV - 1;
 #pragma unroll
           for (int q = EPV - 1; q >= 0; --q)
-            if (x[q] == vm) jj = q;
-          bidx = e0 + jj;
+            if (x[j][q] == vm[j]) jj = q;
+          bidx = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + j * NT + tid) * EPV) + jj;
         }
-        if (track_min) {
+      }
+      if (track_min) {
+#pragma unroll
+        for (int j = 0; j < VPT; ++j)
 #pragma unroll
           for (int q = 0; q < EPV; ++q)
-            if (x[q] > -INFINITY) mnv = fminf(mnv, x[q]);
-        }
-        if (filtering) {
-          // one warp-aggregated append per vector: scan the lanes' survivor counts, reserve once
-          uint32_t pm = 0;
+            if (x[j][q] > -INFINITY) mnv = fminf(mnv, x[j][q]);
+      }
+      if (filtering && !row_ovf) {
+        if (!have_thr) {
+          // exact first threshold: the k-th largest value of this first chunk
+          const int n0 = nv * EPV;
+          if (n0 >= top_k) {
+            uint32_t kk[VPT * EPV];
+            uint32_t mn = 0xFFFFFFFFu, mx = 0;
 #pragma unroll
-          for (int q = 0; q < EPV; ++q)
-            if (valid && x[q] >= t) pm |= 1u << q;
-          const uint32_t cnt = (uint32_t)__popc(pm);
-          if (__any_sync(0xFFFFFFFFu, cnt != 0)) {
-            const uint32_t incl = warp_incl_scan(cnt);
-            uint32_t base = 0;
-            if ((tid & 31) == 31) base = (uint32_t)atomicAdd(&sh.cand_n, (int)incl);
-            base = __shfl_sync(0xFFFFFFFFu, base, 31);
-            uint32_t pos = base + incl - cnt;
+            for (int j = 0; j < VPT; ++j)
 #pragma unroll
-            for (int q = 0; q < EPV; ++q) {
-              if ((pm >> q) & 1u) {
-                if (pos < (uint32_t)CAND_CAP) candB[pos] = compose(key_of(x[q]), e0 + q);
-                ++pos;
+              for (int q = 0; q < EPV; ++q) {
+                const bool ok = j * NT + tid < nv;
+                kk[j * EPV + q] = ok ? key_of(x[j][q]) : 0u;
+                if (ok) mn = min(mn, kk[j * EPV + q]);
+                mx = max(mx, kk[j * EPV + q]);
               }
-            }
+            uint32_t unused, kmin, kmax;
+            block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+            const uint32_t k0 = block_kth_select<VPT * EPV>(kk, (uint32_t)top_k, kmin, (uint32_t)n0,
+                                                            (uint64_t)kmax + 1, false, sh);
+            if (tid == 0) sh.thr_f = tie_floor(value_of(k0), tf);
+          }
+          __syncthreads();
+          have_thr = true;
+        }
+        const float t = sh.thr_f;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          if (vm[j] >= t) {
+            const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + j * NT + tid) * EPV);
+#pragma unroll
+            for (int q = 0; q < EPV; ++q)
+              if (x[j][q] >= t) push(x[j][q], e0 + q);
           }
         }
       }
-      __syncthreads();
+      // every thread is done with this stage: refill it, then compact if a thread's slots are half full
+      const int crowded = __syncthreads_or(filtering && nc >= SLOTS / 2);
       if (tid == 0 && c + NSTAGE < nchunks) {
         const uint64_t pol = keep_in_l2 ? l2_policy_evict_last() : l2_policy_evict_first();
         const int64_t cn = c + NSTAGE;
@@ -786,7 +847,10 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         mbar_expect_tx(&sh.mbar[stage], (uint32_t)(nv2 * 16));
         bulk_load(ring + stage * CHUNK_VEC, src + cn * CHUNK_VEC, (uint32_t)(nv2 * 16), &sh.mbar[stage], pol);
       }
-      if (filtering && !sh.overflow && sh.cand_n >= CAND_HI) compact(top_k);
+      if (filtering) {
+        if (__syncthreads_or(ovf)) row_ovf = true;
+        if (crowded && !row_ovf) compact(top_k);
+      }
     }
     if (sh.timeout) {
       // let every issued copy land before the shared memory is reused
@@ -800,18 +864,31 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       __syncthreads();
     }
   }
-  for (int64_t t0 = 0; t0 < s.tail_n; t0 += NT) {
-    const int64_t e = s.tail_e0 + t0 + tid;
-    const bool valid = t0 + tid < s.tail_n;
-    float x = -INFINITY;
-    if (valid) x = Elem<T>::ld(row + e);
-    visit1(valid, x, (uint32_t)e, sh.thr_f);
+  for (int64_t e = tid; e < s.tail_n; e += NT) visit1(Elem<T>::ld(row + s.tail_e0 + e), (uint32_t)(s.tail_e0 + e));
+  if (filtering) {
+    // head and tail elements against the final threshold
+    __syncthreads();
+    const float t = sh.thr_f;
+    for (int64_t e = tid; e < s.head_n; e += NT) {
+      const float x = Elem<T>::ld(row + e);
+      if (x >= t) push(x, (uint32_t)e);
+    }
+    for (int64_t e = tid; e < s.tail_n; e += NT) {
+      const float x = Elem<T>::ld(row + s.tail_e0 + e);
+      if (x >= t) push(x, (uint32_t)(s.tail_e0 + e));
+    }
+    if (__syncthreads_or(ovf)) row_ovf = true;
+    if (!row_ovf) {
+      // shrink the list to this slice's top_k (plus ties), then pack it densely into the idle ring
+      compact(top_k);
+      uint32_t tot;
+      const uint32_t pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
+      uint64_t* dense = reinterpret_cast<uint64_t*>(regA);
+      for (int j = 0; j < nc; ++j) dense[pos + j] = candB[j * NT + tid];
+      if (tid == 0) sh.cand_n = (int32_t)tot;
+    }
+    if (tid == 0) sh.overflow = row_ovf ? 1 : 0;
   }
-  __syncthreads();
-  if (filtering && !sh.overflow && sh.cand_n > CAND_CAP) sh.overflow = 1;
-  __syncthreads();
-  // with more than one CTA per row, shrink each list to its local survivors before the merge
-  if (filtering && C > 1 && !sh.overflow && sh.cand_n > top_k) compact(top_k);
 
   // CTA reduction: (first maximum, its index), NaN-propagating max, smallest value above -inf
   {
@@ -847,7 +924,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       sh.pub_max = runmax;
       sh.pub_idx = bidx;
       sh.pub_mnv = mnv;
-      sh.pub_cand_n = min(sh.cand_n, CAND_CAP);
+      sh.pub_cand_n = (filtering && !sh.overflow) ? sh.cand_n : 0;
       sh.pub_overflow = sh.overflow;
       sh.pub_timeout = sh.timeout;
     }
@@ -942,25 +1019,43 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     uint64_t* K = reinterpret_cast<uint64_t*>(regA + NBIN * 24);
     zero_probs();
     if (rank == 0) {
-      uint64_t* lists[8];
-      int32_t counts[8];
+      // concatenate the CTAs' packed lists (rank r's list sits at the start of its ring)
+      int32_t counts[8], offs[8];
       int32_t total = 0;
       for (int r = 0; r < C; ++r) {
-        lists[r] = cluster.map_shared_rank(candB, r);
         counts[r] = cluster.map_shared_rank(&sh, r)->pub_cand_n;
+        offs[r] = total;
         total += counts[r];
       }
-      const uint32_t kth_raw = block_kth_key(lists, counts, C, min(top_k, total), sh);
-      const uint32_t kth = key_of(__fdiv_rn(value_of(kth_raw), tf));
-      if (tid == 0) sh.nk = 0;
+      const bool fits = total > 0 && total <= CAND_CAP;
+      if (fits) {
+        for (int r = 0; r < C; ++r) {
+          const uint64_t* L = cluster.map_shared_rank(reinterpret_cast<uint64_t*>(regA), r);
+          for (int i = tid; i < counts[r]; i += NT) candB[offs[r] + i] = L[i];
+        }
+      }
+      if (tid == 0) sh.nk = fits ? 0 : KCAP + 1;
       __syncthreads();
-      for (int r = 0; r < C; ++r) {
-        const uint64_t* L = lists[r];
-        for (int i0 = 0; i0 < counts[r]; i0 += NT) {
+      if (fits) {
+        uint32_t kk[SLOTS];
+        uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+          const int i = j * NT + tid;
+          kk[j] = (i < total) ? comp_key(candB[i]) : 0u;
+          if (i < total) mn = min(mn, kk[j]);
+          mx = max(mx, kk[j]);
+        }
+        uint32_t unused, kmin, kmax;
+        block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+        const uint32_t kth_raw = block_kth_select<SLOTS>(kk, (uint32_t)min(top_k, total), kmin, (uint32_t)total,
+                                                         (uint64_t)kmax + 1, true, sh);
+        const uint32_t kth = key_of(__fdiv_rn(value_of(kth_raw), tf));
+        for (int i0 = 0; i0 < total; i0 += NT) {
           const int i = i0 + tid;
-          const uint64_t c = (i < counts[r]) ? L[i] : 0ull;
-          const uint32_t k = (c != 0ull) ? key_of(__fdiv_rn(value_of(comp_key(c)), tf)) : 0u;
-          warp_append(c != 0ull && k >= kth, k, comp_idx(c), K, &sh.nk, KCAP);
+          const uint64_t c = (i < total) ? candB[i] : 0ull;
+          const uint32_t k = (i < total) ? key_of(__fdiv_rn(value_of(comp_key(c)), tf)) : 0u;
+          warp_append(i < total && k >= kth, k, comp_idx(c), K, &sh.nk, KCAP);
         }
       }
       __syncthreads();
