@@ -829,7 +829,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         const float t = sh.thr_f;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
-          if (vm[j] >= t) {
+          if (j * NT + tid < nv && vm[j] >= t) {  // vectors past the chunk's end hold -inf padding
             const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + j * NT + tid) * EPV);
 #pragma unroll
             for (int q = 0; q < EPV; ++q)

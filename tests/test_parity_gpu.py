@@ -133,6 +133,32 @@ def test_config2_flat_worst_case():
     compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label="cfg2flat")
 
 
+@pytest.mark.parametrize("cluster", ["1", "2"])
+def test_long_rows(cluster):
+    """Slices longer than the per-thread group slots (they fold), k up to the small-path limit."""
+    os.environ["PB_CLUSTER"] = cluster
+    rng = np.random.default_rng(11)
+    for V, dtype in ((300_001, torch.float32), (600_000, torch.bfloat16)):
+        x = workloads.head_boosted(4, V, seed=V).to(dtype)
+        rec = oracle.make_params([0.7, 1.0, 1.0, 1.3], [0.95, 1.0, 0.9, 1.0], [50, 1000, 7, 1024], rng.random(4))
+        compare(x, rec, label=f"long V={V} C={cluster}")
+
+
+@pytest.mark.parametrize("cluster", ["1", "8"])
+def test_rows_with_fewer_finite_values_than_k(cluster):
+    """The k-th value is -inf: every -inf element is kept (weight 0) and none is ever drawn."""
+    os.environ["PB_CLUSTER"] = cluster
+    rng = np.random.default_rng(5)
+    V = 4099
+    x = torch.full((4, V), float("-inf"))
+    for r, n in enumerate((1, 37, 500, 999)):
+        cols = torch.from_numpy(rng.choice(V, n, replace=False))
+        x[r, cols] = torch.randn(n, generator=torch.Generator().manual_seed(r)) * 2.0
+    rec = oracle.make_params([1.0, 0.7, 1.0, 1.3], [1.0, 0.9, 1.0, 0.5], [1000, 1000, 1000, 1000], rng.random(4))
+    tok, info = compare(x, rec, label=f"sparse-finite C={cluster}")
+    assert np.all(np.isfinite(x.numpy()[np.arange(4), tok]))
+
+
 def test_large_tie_groups():
     """Rows with one repeated value (tie groups far above the gather buffer) and few distinct values."""
     V = 20000
