@@ -266,7 +266,7 @@ def run_ours(args):
                    "l2": f"{NROT} rotating input copies ({NROT * alg_bytes / 1e6:.0f} MB > 126 MB L2)",
                    "timing": "CUDA graph of K launches between CUDA events, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": load_traffic(w.name),
                      "alg_bytes_per_launch": alg_bytes},
         "e2e": {"value": world * B / e2e_s, "unit": "rows/s", "ms_per_step": e2e_s * 1e3,
                 "h2d_bytes_per_step": alg_bytes + rec.nbytes, "d2h_bytes_per_step": 8 * B,
@@ -284,6 +284,16 @@ def run_ours(args):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def load_traffic(workload):
+    """DRAM bytes (read + write) of one launch on this workload, from a committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload, {}).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
 
 
 def main():
