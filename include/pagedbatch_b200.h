@@ -63,6 +63,9 @@ extern "C" {
 #define PB_ROW_INTERNAL 8    /* a selection found no element for its target (an internal error) */
 #define PB_ROW_BAD_PARAMS 16 /* temperature < 0 or NaN, top_p outside (0, 1], or top_k < 0
                                 (values SamplingParams rejects, config.py:146-155) */
+#define PB_ROW_FALLBACK 32   /* pb_merge only: the shards' candidates cannot settle this row
+                                (top-k off or above the record, or a tie group overflowing it);
+                                sample it from its full row with pb_sample */
 
 /* pb_row_info.flags: which path resolved the row (diagnostic) */
 #define PB_PATH_GREEDY 1
@@ -108,6 +111,49 @@ typedef struct pb_row_info {
 PB_API int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
                      const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
                      pb_row_info* out_info, float* out_probs, void* stream);
+
+/*
+ * Vocabulary-parallel sampling (rows split by columns over N shards, as the output of a
+ * tensor-parallel LM head). No counterpart in the reference, which samples whole rows; the result
+ * is the same as pb_sample on the full rows: the union of every shard's top-k survivors (all
+ * values >= the shard's k-th, ties kept) contains the row's top-k set and its max.
+ *
+ *   1. pb_candidates on every shard writes one fixed-size record per row;
+ *   2. the caller all-gathers the records of the N shards (records[s][row], s = shard order);
+ *   3. pb_merge on any shard turns the N records of each row into its token and pb_row_info.
+ * Rows the records cannot settle come back with status PB_ROW_FALLBACK.
+ */
+
+/* Header of one row's record; `count` uint64 entries follow (key << 32 | (0xFFFFFFFF - index)). */
+typedef struct pb_cand_header {
+  int32_t count;   /* entries that follow */
+  int32_t flags;   /* PB_ROW_* status of the shard's row (low byte) | PB_CAND_* */
+  float max_key;   /* shard's largest scaled key (raw logit for greedy rows) */
+  int32_t reserved;
+} pb_cand_header;
+#define PB_CAND_FALLBACK 0x100 /* this shard cannot describe its part of the row */
+#define PB_CAND_GREEDY 0x200   /* one entry: the shard's first maximum (raw key) */
+#define PB_CAND_MAX_CAP 2048   /* largest entries per record */
+
+/* Bytes of one row's record for `cap` entries (16 + 8 * cap). */
+PB_API int64_t pb_record_bytes(int32_t cap);
+
+/*
+ * Local half of a vocabulary-parallel step on one shard: columns [vocab_offset, vocab_offset +
+ * shard_vocab) of every row. Arguments as pb_sample; `params` are the rows' full parameters (the
+ * top_k of the whole row); out_records holds n_rows records of pb_record_bytes(cap) bytes.
+ */
+PB_API int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t row_stride,
+                         const int32_t* row_index, const pb_row_params* params, int64_t vocab_offset, int32_t cap,
+                         void* out_records, void* stream);
+
+/*
+ * Merge: records laid out [n_shards][n_rows][pb_record_bytes(cap)], shards in column order.
+ * Writes out_token (-1 unless PB_ROW_OK) and optional out_info exactly as pb_sample would for the
+ * full rows, except PB_ROW_FALLBACK rows.
+ */
+PB_API int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,
+                    int64_t* out_token, pb_row_info* out_info, void* stream);
 
 /* Order-preserving 32-bit key of a float (NaN above +inf, -0 == +0); host helper for tests. */
 PB_API uint32_t pb_key_of(float x);

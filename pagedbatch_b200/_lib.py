@@ -19,6 +19,8 @@ PB_OK = 0
 ERRORS = {-1: "invalid argument", -2: "vocabulary too large", -3: "kernel launch failed", -4: "device configuration failed"}
 
 ROW_OK, ROW_NONFINITE, ROW_BAD_UNIFORM, ROW_TIMEOUT, ROW_INTERNAL, ROW_BAD_PARAMS = 0, 1, 2, 4, 8, 16
+ROW_FALLBACK = 32
+CAND_FALLBACK, CAND_GREEDY, CAND_MAX_CAP = 0x100, 0x200, 2048
 PATH_GREEDY, PATH_SMALL, PATH_LARGE = 1, 2, 4
 MAX_VOCAB = 1 << 24
 
@@ -38,9 +40,17 @@ ROW_INFO = np.dtype(
         ("kept_q", "<u8"),
     ]
 )
-assert ROW_PARAMS.itemsize == 32 and ROW_INFO.itemsize == 40
+# struct pb_cand_header (a vocabulary-parallel record starts with it; uint64 entries follow)
+CAND_HEADER = np.dtype([("count", "<i4"), ("flags", "<i4"), ("max_key", "<f4"), ("reserved", "<i4")])
+assert ROW_PARAMS.itemsize == 32 and ROW_INFO.itemsize == 40 and CAND_HEADER.itemsize == 16
 
-EXPORTS = ("pb_sample", "pb_key_of", "pb_exp", "pb_strerror", "pb_version")
+
+def record_bytes(cap: int) -> int:
+    """Bytes of one row's candidate record (pb_record_bytes)."""
+    return CAND_HEADER.itemsize + 8 * int(cap)
+
+EXPORTS = ("pb_sample", "pb_candidates", "pb_merge", "pb_record_bytes", "pb_key_of", "pb_exp", "pb_strerror",
+           "pb_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -67,6 +77,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
     L.pb_sample.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp]
     L.pb_sample.restype = i32
+    L.pb_candidates.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, i32, vp, vp]
+    L.pb_candidates.restype = i32
+    L.pb_merge.argtypes = [vp, i32, i64, i32, vp, vp, vp, vp]
+    L.pb_merge.restype = i32
+    L.pb_record_bytes.argtypes = [i32]
+    L.pb_record_bytes.restype = i64
     L.pb_key_of.argtypes = [ctypes.c_float]
     L.pb_key_of.restype = ctypes.c_uint32
     L.pb_exp.argtypes = [ctypes.c_float]

@@ -67,7 +67,13 @@ struct Args {
   int64_t* out_token;
   pb_row_info* out_info;
   float* out_probs;
+  uint8_t* cand_out;     // vocabulary-parallel shard mode: per-row candidate records (else null)
+  int32_t cand_cap;      // entries per record
+  int64_t vocab_offset;  // global index of this shard's first column
 };
+
+// one row's candidate record: header, then `count` composites (scaled key, global index)
+__host__ __device__ constexpr int64_t record_bytes(int cap) { return (int64_t)sizeof(pb_cand_header) + 8 * (int64_t)cap; }
 
 // decision record broadcast by rank 0 (read by peers through DSMEM)
 struct Dec {
@@ -619,6 +625,81 @@ __device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq,
 
 // ---- the kernel -------------------------------------------------------------------------
 
+// Resolve the survivor list K[0..nk) (composites of scaled key and index, any order, nk <= KCAP)
+// in one CTA: order (key desc, index asc), fixed-point weights, top-p cut, draw. Thread 0 gets the
+// token and the kept-set description; every thread gets sh.found_pos (last kept position) and
+// sh.s64[NW + 1] (kept mass) for the probability write. All threads call.
+__device__ void finish_survivors(uint64_t* K, int nk, float m, bool topp_active, float pf, uint64_t u53, Shared& sh,
+                                 int64_t* token, pb_row_info* info) {
+  const int tid = threadIdx.x;
+  if (nk <= 64) {
+    Finish f;
+    if (tid < 32) warp_finish(K, nk, m, topp_active, pf, u53, &f);
+    if (tid == 0) sh.fin = f;
+    __syncthreads();
+    f = sh.fin;
+    if (tid == 0) {
+      if (!f.ok) info->status = PB_ROW_INTERNAL;
+      *token = f.token;
+      info->thr_key = f.thr_key;
+      info->n_tie_kept = f.n_tie;
+      info->kept_count = f.last + 1;
+      info->z_q = f.zq;
+      info->kept_q = f.kept;
+      info->flags = PB_PATH_SMALL;
+      sh.nk = nk;
+      sh.found_pos = f.last;
+      sh.s64[NW + 1] = f.kept;
+    }
+    __syncthreads();
+    return;
+  }
+  block_sort_desc(K, nk);
+  uint64_t zq;
+  {
+    const int seg = (nk + NT - 1) / NT;
+    const int p0 = min(nk, tid * seg), p1 = min(nk, p0 + seg);
+    uint64_t sum = 0;
+    for (int p = p0; p < p1; ++p) sum += weight_q(value_of(comp_key(K[p])), m);
+    block_excl_scan<uint64_t, NT>(sum, sh.s64, &zq);
+  }
+  int last = nk - 1;
+  uint64_t kept = zq;
+  bool ok = true;
+  if (topp_active) {
+    list_find(K, nk, MODE_MASS, m, 0, mul_floor(pf, zq), sh);
+    last = sh.found_pos;
+    kept = sh.found_incl;
+    ok = last >= 0;
+  }
+  int pick = -1;
+  if (ok) {
+    list_find(K, nk, MODE_MASS, m, 0, scale_u53(u53, kept), sh);
+    pick = sh.found_pos;
+    ok = pick >= 0;
+  }
+  if (!ok) {
+    last = 0;
+    pick = 0;
+    if (tid == 0) info->status = PB_ROW_INTERNAL;
+  }
+  __syncthreads();  // every thread has read sh.found_pos
+  if (tid == 0) {
+    *token = comp_idx(K[pick]);
+    const uint32_t tk = comp_key(K[last]);
+    info->thr_key = tk;
+    info->n_tie_kept = last - first_of_key(K, nk, tk) + 1;
+    info->kept_count = last + 1;
+    info->z_q = zq;
+    info->kept_q = kept;
+    info->flags = PB_PATH_SMALL;
+    sh.nk = nk;
+    sh.found_pos = last;
+    sh.s64[NW + 1] = kept;
+  }
+  __syncthreads();
+}
+
 template <typename T>
 __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
@@ -963,6 +1044,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   info.max_key = (greedy && sh.row_max == sh.row_max) ? sh.row_best : m;
   int64_t token = -1;
   bool finished = false;
+  pb_cand_header cand_hdr = {0, PB_CAND_FALLBACK, 0.0f, 0};  // shard mode: what this row publishes
 
   auto zero_probs = [&]() {
     if (prow)
@@ -1003,7 +1085,8 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     if (prow && rank == 0 && tid == 0) prow[token] = 1.0f;
     finished = true;
   } else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) {
-    info.status = PB_ROW_NONFINITE;
+    // a shard whose values are all -inf cannot tell whether the whole row is: it defers
+    if (!(a.cand_out && mk <= KEY_NEG_INF)) info.status = PB_ROW_NONFINITE;
     finished = true;
   } else if (!(sh.uniform >= 0.0 && sh.uniform < 1.0)) {
     info.status = PB_ROW_BAD_UNIFORM;
@@ -1060,71 +1143,22 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       }
       __syncthreads();
       const int nk = sh.nk;
-      if (nk <= 64) {
-        Finish f;
-        if (tid < 32) warp_finish(K, nk, m, topp_active, pf, u53, &f);
-        if (tid == 0) sh.fin = f;
-        __syncthreads();
-        f = sh.fin;
+      if (a.cand_out) {
+        // vocabulary-parallel shard: publish the survivors (global indices) instead of drawing
+        uint8_t* rec = a.cand_out + item * record_bytes(a.cand_cap);
+        uint64_t* ent = reinterpret_cast<uint64_t*>(rec + sizeof(pb_cand_header));
+        const bool fits_rec = nk <= min(a.cand_cap, KCAP);
+        if (fits_rec)
+          for (int i = tid; i < nk; i += NT)
+            ent[i] = compose(comp_key(K[i]), comp_idx(K[i]) + (uint32_t)a.vocab_offset);
         if (tid == 0) {
-          if (!f.ok) info.status = PB_ROW_INTERNAL;
-          token = f.token;
-          info.thr_key = f.thr_key;
-          info.n_tie_kept = f.n_tie;
-          info.kept_count = f.last + 1;
-          info.z_q = f.zq;
-          info.kept_q = f.kept;
-          info.flags = PB_PATH_SMALL;
-          sh.nk = nk;
-          sh.found_pos = f.last;
-          sh.s64[NW + 1] = f.kept;
+          cand_hdr.count = fits_rec ? nk : 0;
+          cand_hdr.flags = fits_rec ? 0 : PB_CAND_FALLBACK;
+          sh.found_pos = -1;
           sh.dec.action = ACT_DONE;
         }
-        __syncthreads();
       } else if (nk <= KCAP) {
-        block_sort_desc(K, nk);
-        uint64_t zq;
-        {
-          const int seg = (nk + NT - 1) / NT;
-          const int p0 = min(nk, tid * seg), p1 = min(nk, p0 + seg);
-          uint64_t sum = 0;
-          for (int p = p0; p < p1; ++p) sum += weight_q(value_of(comp_key(K[p])), m);
-          block_excl_scan<uint64_t, NT>(sum, sh.s64, &zq);
-        }
-        int last = nk - 1;
-        uint64_t kept = zq;
-        bool ok = true;
-        if (topp_active) {
-          list_find(K, nk, MODE_MASS, m, 0, mul_floor(pf, zq), sh);
-          last = sh.found_pos;
-          kept = sh.found_incl;
-          ok = last >= 0;
-        }
-        int pick = -1;
-        if (ok) {
-          list_find(K, nk, MODE_MASS, m, 0, scale_u53(u53, kept), sh);
-          pick = sh.found_pos;
-          ok = pick >= 0;
-        }
-        if (!ok) {
-          last = 0;
-          pick = 0;
-          info.status = PB_ROW_INTERNAL;
-        }
-        if (tid == 0) {
-          token = comp_idx(K[pick]);
-          const uint32_t tk = comp_key(K[last]);
-          info.thr_key = tk;
-          info.n_tie_kept = last - first_of_key(K, nk, tk) + 1;
-          info.kept_count = last + 1;
-          info.z_q = zq;
-          info.kept_q = kept;
-          info.flags = PB_PATH_SMALL;
-          sh.nk = nk;
-          sh.found_pos = last;
-          sh.s64[NW + 1] = kept;
-        }
-        __syncthreads();
+        finish_survivors(K, nk, m, topp_active, pf, u53, sh, &token, &info);
         if (tid == 0) sh.dec.action = ACT_DONE;
       } else {
         if (tid == 0) sh.dec.action = ACT_REFINE;  // too many survivors: cooperative path
@@ -1148,6 +1182,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   }
 
   // ---------------- large path: cooperative histogram selection ----------------
+  if (!finished && a.cand_out) finished = true;  // shard mode: such rows fall back to full rows
   if (!finished) {
     info.flags = PB_PATH_LARGE;
     uint64_t* G = candB;  // gather list (rank 0)
@@ -1570,7 +1605,23 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     finished = true;
   }
 
-  if (rank == 0 && tid == 0) {
+  if (rank == 0 && tid == 0 && a.cand_out) {
+    uint8_t* rec = a.cand_out + item * record_bytes(a.cand_cap);
+    pb_cand_header* h = reinterpret_cast<pb_cand_header*>(rec);
+    if (info.status != PB_ROW_OK) {
+      cand_hdr.count = 0;
+      cand_hdr.flags = info.status;
+    } else if (greedy) {
+      reinterpret_cast<uint64_t*>(rec + sizeof(pb_cand_header))[0] =
+          compose(key_of(info.max_key), (uint32_t)token + (uint32_t)a.vocab_offset);
+      cand_hdr.count = 1;
+      cand_hdr.flags = PB_CAND_GREEDY;
+    }
+    h->count = cand_hdr.count;
+    h->flags = cand_hdr.flags;
+    h->max_key = info.max_key;
+    h->reserved = 0;
+  } else if (rank == 0 && tid == 0) {
     a.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
     if (a.out_info) {  // field by field: records sit at 40-byte strides
       pb_row_info* o = a.out_info + item;
@@ -1585,6 +1636,155 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     }
   }
   cluster.sync();  // no CTA leaves while another may still read its shared memory
+}
+
+// ---- vocabulary-parallel merge -----------------------------------------------------------
+
+constexpr int MERGE_CAP = 4096;  // union entries one row's merge resolves in shared memory
+constexpr int MERGE_SMEM = MERGE_CAP * 8 + KCAP * 8;
+
+struct MergeArgs {
+  const uint8_t* records;  // [n_shards][n_rows][record_bytes(cap)]
+  int32_t n_shards;
+  int64_t n_rows;
+  int32_t cap;
+  const pb_row_params* params;
+  int64_t* out_token;
+  pb_row_info* out_info;
+};
+
+// One CTA per row: the row's token from the union of its shards' survivors, by the same steps and
+// arithmetic as the small path of sample_kernel (exact k-th key, fixed-point weights, top-p cut,
+// inverse-CDF draw), so the result equals sampling the full row.
+__global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
+  extern __shared__ __align__(128) unsigned char dyn[];
+  __shared__ Shared sh;
+  uint64_t* L = reinterpret_cast<uint64_t*>(dyn);                  // the union of the records
+  uint64_t* K = reinterpret_cast<uint64_t*>(dyn + MERGE_CAP * 8);  // the row's survivors
+  const int64_t item = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int64_t rb = record_bytes(a.cap);
+  auto header = [&](int r) {
+    return reinterpret_cast<const pb_cand_header*>(a.records + ((int64_t)r * a.n_rows + item) * rb);
+  };
+  auto entries = [&](int r) { return reinterpret_cast<const uint64_t*>(header(r) + 1); };
+
+  if (tid == 0) {
+    const pb_row_params p = a.params[item];
+    sh.temperature = p.temperature;
+    sh.top_p = p.top_p;
+    sh.uniform = p.uniform;
+    sh.top_k = p.top_k;
+    sh.greedy = (p.temperature == 0.0);
+    sh.tf = (float)p.temperature;
+    int32_t fl = 0, total = 0;
+    float gmax = -INFINITY;
+    uint64_t best = 0;
+    int best_r = 0;
+    for (int r = 0; r < a.n_shards; ++r) {
+      const pb_cand_header* h = header(r);
+      fl |= h->flags;
+      total += h->count;
+      gmax = fmax_nan(gmax, h->max_key);
+      if ((h->flags & PB_CAND_GREEDY) && h->count == 1 && entries(r)[0] > best) {
+        best = entries(r)[0];
+        best_r = r;
+      }
+    }
+    sh.status = PB_ROW_OK;
+    const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
+    const uint32_t mk = key_of(gmax);
+    int mode = 0;  // 0 status only, 1 greedy, 2 merge
+    if (fl & PB_ROW_TIMEOUT) sh.status = PB_ROW_TIMEOUT;
+    else if (bad) sh.status = PB_ROW_BAD_PARAMS;
+    else if (sh.greedy) mode = 1;
+    else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) sh.status = PB_ROW_NONFINITE;
+    else if (!(p.uniform >= 0.0 && p.uniform < 1.0)) sh.status = PB_ROW_BAD_UNIFORM;
+    else if ((fl & (PB_CAND_FALLBACK | 0xFF)) || total > MERGE_CAP || total == 0) sh.status = PB_ROW_FALLBACK;
+    else mode = 2;
+    if (mode == 1 && (fl & ~PB_CAND_GREEDY)) {  // a shard could not publish its maximum
+      sh.status = PB_ROW_FALLBACK;
+      mode = 0;
+    }
+    sh.cand_n = total;
+    sh.nk = mode;
+    sh.row_max = gmax;
+    sh.row_best = header(best_r)->max_key;
+    sh.arg = comp_idx(best);
+    sh.mk = key_of(gmax);
+  }
+  __syncthreads();
+  const int mode = sh.nk;
+  pb_row_info info = {};
+  int64_t token = -1;
+  info.status = sh.status;
+  if (mode == 1) {
+    info.max_key = sh.row_best;
+    info.thr_key = key_of(info.max_key);
+    info.n_tie_kept = 1;
+    info.kept_count = 1;
+    info.flags = PB_PATH_GREEDY;
+    token = sh.arg;
+  } else if (mode == 2) {
+    const float m = sh.row_max;
+    const int total = sh.cand_n;
+    const int32_t top_k = sh.top_k;
+    info.max_key = m;
+    // gather the union (shards in order; entry order does not matter)
+    int off = 0;
+    for (int r = 0; r < a.n_shards; ++r) {
+      const int n = header(r)->count;
+      const uint64_t* e = entries(r);
+      for (int i = tid; i < n; i += NT) L[off + i] = e[i];
+      off += n;
+    }
+    __syncthreads();
+    uint32_t kk[MERGE_CAP / NT];
+    uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+    for (int j = 0; j < MERGE_CAP / NT; ++j) {
+      const int i = j * NT + tid;
+      kk[j] = (i < total) ? comp_key(L[i]) : 0u;
+      if (i < total) mn = min(mn, kk[j]);
+      mx = max(mx, kk[j]);
+    }
+    uint32_t unused, kmin, kmax;
+    block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+    const int kq = (top_k > 0) ? min(top_k, total) : total;
+    const uint32_t kth = block_kth_select<MERGE_CAP / NT>(kk, (uint32_t)kq, kmin, (uint32_t)total, (uint64_t)kmax + 1,
+                                                          true, sh);
+    if (tid == 0) sh.nk = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < total; i0 += NT) {
+      const int i = i0 + tid;
+      const uint64_t c = (i < total) ? L[i] : 0ull;
+      warp_append(i < total && comp_key(c) >= kth, comp_key(c), comp_idx(c), K, &sh.nk, KCAP);
+    }
+    __syncthreads();
+    const int nk = sh.nk;
+    if (nk <= KCAP) {
+      const bool topp_active = sh.top_p < 1.0 && (float)sh.top_p < 1.0f;
+      finish_survivors(K, nk, m, topp_active, (float)sh.top_p, (uint64_t)(sh.uniform * 0x1p53), sh, &token, &info);
+    } else if (tid == 0) {
+      info.status = PB_ROW_FALLBACK;
+    }
+  } else if (sh.status == PB_ROW_NONFINITE || sh.status == PB_ROW_BAD_UNIFORM || sh.status == PB_ROW_TIMEOUT) {
+    info.max_key = sh.row_max;
+  }
+  if (tid == 0) {
+    a.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
+    if (a.out_info) {
+      pb_row_info* o = a.out_info + item;
+      o->thr_key = info.thr_key;
+      o->n_tie_kept = info.n_tie_kept;
+      o->kept_count = info.kept_count;
+      o->status = info.status;
+      o->max_key = info.max_key;
+      o->flags = info.flags;
+      o->z_q = info.z_q;
+      o->kept_q = info.kept_q;
+    }
+  }
 }
 
 template <typename T>
@@ -1663,11 +1863,77 @@ int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int6
   a.out_token = out_token;
   a.out_info = out_info;
   a.out_probs = out_probs;
+  a.cand_out = nullptr;
+  a.cand_cap = 0;
+  a.vocab_offset = 0;
   const int C = cluster_size_for(n_rows, vocab, es);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
   if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
   return launch<__half>(a, C, st);
+}
+
+int64_t pb_record_bytes(int32_t cap) { return record_bytes(cap); }
+
+int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t row_stride,
+                  const int32_t* row_index, const pb_row_params* params, int64_t vocab_offset, int32_t cap,
+                  void* out_records, void* stream) {
+  if (n_rows < 0 || shard_vocab <= 0 || row_stride < shard_vocab || vocab_offset < 0) return PB_E_INVALID;
+  if (cap < 1 || cap > PB_CAND_MAX_CAP) return PB_E_INVALID;
+  if (vocab_offset + shard_vocab >= PB_MAX_VOCAB) return PB_E_TOO_LARGE;
+  if (n_rows == 0) return PB_OK;
+  if (!logits || !params || !out_records) return PB_E_INVALID;
+  if (n_rows > (int64_t)(0x7FFFFFFF / 8)) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(out_records) & 15) != 0) return PB_E_INVALID;
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  Args a;
+  a.logits = static_cast<const char*>(logits);
+  a.n_rows = n_rows;
+  a.vocab = shard_vocab;
+  a.row_stride = row_stride;
+  a.row_index = row_index;
+  a.params = params;
+  a.out_token = nullptr;
+  a.out_info = nullptr;
+  a.out_probs = nullptr;
+  a.cand_out = static_cast<uint8_t*>(out_records);
+  a.cand_cap = cap;
+  a.vocab_offset = vocab_offset;
+  const int C = cluster_size_for(n_rows, shard_vocab, es);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
+  if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
+  return launch<__half>(a, C, st);
+}
+
+int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,
+             int64_t* out_token, pb_row_info* out_info, void* stream) {
+  if (n_shards < 1 || n_shards > 64 || n_rows < 0 || cap < 1 || cap > PB_CAND_MAX_CAP) return PB_E_INVALID;
+  if (n_rows == 0) return PB_OK;
+  if (!records || !params || !out_token) return PB_E_INVALID;
+  if (n_rows > (int64_t)0x7FFFFFFF) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(records) & 15) != 0) return PB_E_INVALID;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_SMEM) != cudaSuccess)
+      return PB_E_DEVICE;
+    configured |= 1ull << dev;
+  }
+  MergeArgs m;
+  m.records = static_cast<const uint8_t*>(records);
+  m.n_shards = n_shards;
+  m.n_rows = n_rows;
+  m.cap = cap;
+  m.params = params;
+  m.out_token = out_token;
+  m.out_info = out_info;
+  merge_kernel<<<(unsigned)n_rows, NT, MERGE_SMEM, static_cast<cudaStream_t>(stream)>>>(m);
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  return PB_OK;
 }
 
 uint32_t pb_key_of(float x) {

@@ -135,7 +135,7 @@ def test_config2_flat_worst_case():
 
 @pytest.mark.parametrize("cluster", ["1", "2"])
 def test_long_rows(cluster):
-    """Slices longer than the per-thread group slots (they fold), k up to the small-path limit."""
+    """Rows far longer than the TMA ring, bf16 and fp32, k up to the small-path limit."""
     os.environ["PB_CLUSTER"] = cluster
     rng = np.random.default_rng(11)
     for V, dtype in ((300_001, torch.float32), (600_000, torch.bfloat16)):
@@ -226,3 +226,75 @@ def test_seeded_sampling_is_reproducible():
     assert a == b
     with pytest.raises(RuntimeError, match="nan"):
         sample_tokens(torch.full((1, 8), float("nan"), device="cuda"), [SamplingParams()], [torch.Generator()])
+
+
+@pytest.mark.parametrize("n_shards", [2, 4, 8])
+def test_vocab_parallel_shards_match_full_rows(n_shards):
+    """Shard candidates + merge (one GPU standing in for N shards) equal the full-row sampler."""
+    from pagedbatch_b200 import SamplingParams
+    from pagedbatch_b200.vocab_parallel import CudaKernels, record_cap
+
+    kern = CudaKernels()
+    cases = []
+    w3 = workloads.config3(rows=128)
+    cases.append((w3.logits, w3.params, w3.uniforms()))
+    w1 = workloads.config1(rows=64)
+    cases.append((w1.logits, w1.params, w1.uniforms()))
+    x = workloads.head_boosted(8, 9001, seed=9)
+    x[3, ::5] = 2.5  # a large tie group
+    ps = [SamplingParams(temperature=t, top_k=k, top_p=p) for t, k, p in
+          [(0.7, 50, 0.95), (1.0, 1, 1.0), (0.0, 0, 1.0), (1.0, 64, 0.9), (1.3, 200, 0.5), (0.5, 20, 1e-6),
+           (1.0, 0, 0.9), (2.0, 7, 1.0)]]
+    cases.append((x, ps, list(np.random.default_rng(4).random(8))))
+    for logits, params, u in cases:
+        dev = logits.cuda()
+        B, V = dev.shape
+        rec = oracle.make_params([p.temperature for p in params], [p.top_p for p in params],
+                                 [p.top_k for p in params], u)
+        dparams = ops.params_tensor(rec, dev.device)
+        cap = record_cap(params)
+        bounds = [V * s // n_shards for s in range(n_shards + 1)]
+        recs = [kern.candidates(dev[:, bounds[s]:bounds[s + 1]], dparams, bounds[s], cap) for s in range(n_shards)]
+        tok, info = kern.merge(torch.stack(recs), dparams, cap)
+        g_tok = tok.cpu().numpy()
+        g_info = ops.info_records(info)
+        f_tok, f_info, _ = ops.sample(dev, dparams, None, with_info=True)
+        f_tok = f_tok.cpu().numpy()
+        f_info = ops.info_records(f_info)
+        fb = g_info["status"] == _lib.ROW_FALLBACK
+        ks = np.array([p.top_k for p in params])
+        greedy = np.array([p.temperature == 0 for p in params])
+        assert not fb[greedy].any()
+        assert fb[(ks == 0) & ~greedy].all()
+        ok = ~fb
+        assert np.array_equal(g_tok[ok], f_tok[ok]), (np.flatnonzero(g_tok[ok] != f_tok[ok]))
+        for f in INFO_FIELDS:
+            assert np.array_equal(g_info[f][ok], f_info[f][ok]), f
+        assert np.array_equal(g_info["max_key"][ok], f_info["max_key"][ok], equal_nan=True)
+        if logits is w3.logits:
+            assert not fb.any()  # config 3 (top_k 64) never needs full rows
+
+
+def test_vocab_parallel_api_one_rank_nccl():
+    """The public entry through a real (one-rank) NCCL group, against sample_tokens."""
+    import socket
+
+    import torch.distributed as dist
+
+    from pagedbatch_b200 import sample_tokens
+    from pagedbatch_b200.vocab_parallel import sample_tokens_vocab_parallel
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        w = workloads.config1(rows=32)
+        x = w.logits.cuda()
+        a = sample_tokens_vocab_parallel(x, w.params, w.generators())
+        b = sample_tokens(x, w.params, w.generators())
+        assert a == b
+    finally:
+        dist.destroy_process_group()
