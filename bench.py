@@ -55,7 +55,7 @@ def load_peaks():
 
 def make_workload(name: str, rank: int):
     fn = {"cfg0": workloads.config0, "cfg1": workloads.config1, "cfg2": workloads.config2,
-          "cfg2flat": workloads.config2_flat}[name]
+          "cfg2flat": workloads.config2_flat, "cfg3": workloads.config3}[name]
     return fn(seed=rank)
 
 
@@ -154,6 +154,88 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_vocab_parallel(args):
+    """Config 3: each rank holds a column slice of [1024, 128256] bf16; shard candidates, one NCCL
+    all-gather of the per-row records, merge. Strong scaling (the job is fixed as N grows)."""
+    from pagedbatch_b200.vocab_parallel import CudaKernels, record_cap
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _lib.load()
+    w = workloads.config3(seed=0)
+    B, V = w.logits.shape
+    lo, hi = V * rank // world, V * (rank + 1) // world
+    xs = [w.logits[:, lo:hi].contiguous().to(dev) for _ in range(NROT)]
+    rec = sampling.pack_rows(w.params, np.array(w.uniforms()))
+    dparams = ops.params_tensor(rec, dev)
+    cap = record_cap(w.params)
+    kern = CudaKernels()
+    rb = _lib.record_bytes(cap)
+    gathered = torch.empty((world, B, rb), dtype=torch.uint8, device=dev)
+
+    def step(i):
+        mine = kern.candidates(xs[i % NROT], dparams, lo, cap)
+        if dist:
+            dist.all_gather_into_tensor(gathered.view(world * B, rb), mine)
+            return kern.merge(gathered, dparams, cap)
+        return kern.merge(mine.unsqueeze(0), dparams, cap)
+
+    for i in range(args.warmup):
+        tok, info = step(i)
+    torch.cuda.synchronize(dev)
+    fallback = int((ops.info_records(info)["status"] == _lib.ROW_FALLBACK).sum())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev0.record()
+        for i in range(args.steps):
+            step(i)
+        ev1.record()
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    step_ms = ms_max / args.steps
+    peak, peak_kind = load_peaks()
+    shard_bytes = B * (hi - lo) * 2
+    line = {
+        "metric": "vocab-parallel sampled rows/s at B=1024,V=128256 bf16 (config 3); 1/2/4/8 GPU",
+        "value": B * args.steps / (ms_max / 1e3), "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": w.name, "rows": B, "vocab": V, "shard_vocab": hi - lo,
+                   "parallelism": f"vocab-parallel over {world} rank(s): one NCCL all-gather of {rb} B per row per rank",
+                   "l2": f"{NROT} rotating input copies ({NROT * shard_bytes / 1e6:.0f} MB per rank)",
+                   "timing": "eager launches between CUDA events, max over ranks", "fallback_rows": fallback},
+        "roofline": {"bound": "hbm", "achieved": shard_bytes / (step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": shard_bytes / (step_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": None, "alg_bytes_per_launch": shard_bytes},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_ours(args):
@@ -302,7 +384,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg0", "cfg1", "cfg2", "cfg2flat"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg0", "cfg1", "cfg2", "cfg2flat", "cfg3"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="eager launches only (for ncu), no timing")
     args = ap.parse_args()
@@ -310,6 +392,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg3":
+        run_vocab_parallel(args)
     else:
         run_ours(args)
 
