@@ -105,7 +105,11 @@ struct alignas(16) Finish {
 };
 
 struct Shared {
-  uint64_t mbar[MAX_STAGE];
+  uint64_t mbar[MAX_STAGE];        // ring stage filled (bulk-copy bytes landed)
+  int64_t stage_chunk[MAX_STAGE];  // last chunk issued into each ring stage
+  uint32_t released[MAX_STAGE];    // warps done with the chunk in each ring stage
+  int32_t cp_flags[3];             // checkpoint flags (timeout 4, overflow 2, crowded 1)
+  uint32_t cp_count[3];            // checkpoint: candidates held by the CTA
   // row parameters
   double temperature, top_p, uniform;
   int32_t top_k, greedy, filtering, status;
@@ -376,7 +380,8 @@ __device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint3
       ge += (b >= mine) ? 1u : 0u;
     }
     const uint32_t r = k - c_hi;
-    if ((uint32_t)lane < n && gt < r && r <= ge) sh.bucket_kth = mine;  // equal keys write the same value
+    const uint32_t hit = __ballot_sync(0xFFFFFFFFu, (uint32_t)lane < n && gt < r && r <= ge);
+    if (hit && lane == __ffs(hit) - 1) sh.bucket_kth = mine;  // lanes that hit hold equal keys
   }
   __syncthreads();
   return sh.bucket_kth;
@@ -625,6 +630,68 @@ __device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq,
 
 // ---- the kernel -------------------------------------------------------------------------
 
+// Raise the candidate threshold sh.thr_f to the tie floor of a lower bound of the kth_rank-th
+// largest candidate held in the per-thread slots (slot j of thread t at candB[j * NT + t]) and
+// drop the candidates below it. Returns this thread's new slot count. All threads call; a barrier
+// separates two calls. Kept out of line so the streaming loop stays small.
+__device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank, float tf, Shared& sh) {
+  const int tid = threadIdx.x;
+  uint32_t kk[SLOTS];
+  uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+  for (int j = 0; j < SLOTS; ++j) {
+    kk[j] = (j < nc) ? comp_key(candB[j * NT + tid]) : 0u;
+    if (j < nc) mn = min(mn, kk[j]);
+    mx = max(mx, kk[j]);
+  }
+  uint32_t tot, kmin, kmax;
+  block_sum_min_max((uint32_t)nc, mn, mx, sh, &tot, &kmin, &kmax);
+  if ((int)tot < kth_rank) return nc;  // fewer candidates than k: nothing to raise
+  // a lower bound of the kth_rank-th candidate (at most BUCKET more candidates above it)
+  const uint32_t kth_raw = block_kth_select<SLOTS>(kk, (uint32_t)kth_rank, kmin, tot, (uint64_t)kmax + 1, false, sh);
+  __syncthreads();  // every thread has read the old threshold
+  if (tid == 0) sh.thr_f = tie_floor(value_of(kth_raw), tf);
+  __syncthreads();
+  const uint32_t fk = key_of(sh.thr_f);
+  int w = 0;
+#pragma unroll
+  for (int j = 0; j < SLOTS; ++j) {
+    if (j < nc && kk[j] >= fk) {
+      candB[w * NT + tid] = candB[j * NT + tid];
+      ++w;
+    }
+  }
+  return w;
+}
+
+// First candidate threshold: sh.thr_f = the tie floor of the top_k-th largest value among the nv
+// staged vectors at buf (thread t owns vectors t, t + NT, ...). All threads call.
+template <typename T, int VPT>
+__device__ __noinline__ void first_threshold(const uint4* buf, int nv, int top_k, float tf, Shared& sh) {
+  constexpr int EPV = Elem<T>::EPV;
+  const int tid = threadIdx.x;
+  uint32_t kk[VPT * EPV];
+  uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const bool ok = j * NT + tid < nv;
+    float x[EPV];
+    if (ok) Elem<T>::unpack(buf[j * NT + tid], x);
+#pragma unroll
+    for (int q = 0; q < EPV; ++q) {
+      kk[j * EPV + q] = ok ? key_of(x[q]) : 0u;
+      if (ok) mn = min(mn, kk[j * EPV + q]);
+      mx = max(mx, kk[j * EPV + q]);
+    }
+  }
+  uint32_t unused, kmin, kmax;
+  block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+  const uint32_t k0 = block_kth_select<VPT * EPV>(kk, (uint32_t)top_k, kmin, (uint32_t)(nv * EPV), (uint64_t)kmax + 1,
+                                                  false, sh);
+  if (tid == 0) sh.thr_f = tie_floor(value_of(k0), tf);
+  __syncthreads();
+}
+
 // Resolve the survivor list K[0..nk) (composites of scaled key and index, any order, nk <= KCAP)
 // in one CTA: order (key desc, index asc), fixed-point weights, top-p cut, draw. Thread 0 gets the
 // token and the kept-set description; every thread gets sh.found_pos (last kept position) and
@@ -747,7 +814,13 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       sh.status = PB_ROW_BAD_PARAMS;
       sh.filtering = 0;
     }
-    for (int st = 0; st < NSTAGE; ++st) mbar_init(&sh.mbar[st], 1);
+    for (int st = 0; st < NSTAGE; ++st) {
+      mbar_init(&sh.mbar[st], 1);
+      sh.stage_chunk[st] = -1;
+      sh.released[st] = 0;
+    }
+    sh.cp_flags[0] = sh.cp_flags[1] = sh.cp_flags[2] = 0;
+    sh.cp_count[0] = sh.cp_count[1] = sh.cp_count[2] = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -782,34 +855,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   // Raise the threshold to the tie floor of the kth_rank-th largest candidate and drop the
   // candidates below it (each thread compacts its own slots). All threads call; a barrier
   // separates two calls.
-  auto compact = [&](int kth_rank) {
-    uint32_t kk[SLOTS];
-    uint32_t mn = 0xFFFFFFFFu, mx = 0;
-#pragma unroll
-    for (int j = 0; j < SLOTS; ++j) {
-      kk[j] = (j < nc) ? comp_key(candB[j * NT + tid]) : 0u;
-      if (j < nc) mn = min(mn, kk[j]);
-      mx = max(mx, kk[j]);
-    }
-    uint32_t tot, kmin, kmax;
-    block_sum_min_max((uint32_t)nc, mn, mx, sh, &tot, &kmin, &kmax);
-    if ((int)tot < kth_rank) return;  // fewer candidates than k: nothing to raise
-    // a lower bound of the kth_rank-th candidate (at most BUCKET more candidates above it)
-    const uint32_t kth_raw = block_kth_select<SLOTS>(kk, (uint32_t)kth_rank, kmin, tot, (uint64_t)kmax + 1, false, sh);
-    __syncthreads();  // every thread has read the old threshold
-    if (tid == 0) sh.thr_f = tie_floor(value_of(kth_raw), tf);
-    __syncthreads();
-    const uint32_t fk = key_of(sh.thr_f);
-    int w = 0;
-#pragma unroll
-    for (int j = 0; j < SLOTS; ++j) {
-      if (j < nc && kk[j] >= fk) {
-        candB[w * NT + tid] = candB[j * NT + tid];
-        ++w;
-      }
-    }
-    nc = w;
-  };
+  auto compact = [&](int kth_rank) { nc = compact_slots(candB, nc, kth_rank, tf, sh); };
   auto visit1 = [&](float x, uint32_t e) {
     runmax = fmax_nan(runmax, x);
     if (x > bestv) {
@@ -826,33 +872,61 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     const uint4* src = reinterpret_cast<const uint4*>(row + s.vec_e0);
     uint4* ring = reinterpret_cast<uint4*>(regA);
     const bool keep_in_l2 = !greedy && !filtering;  // rows that re-read their slice
-    if (tid == 0) {
+    // Warps consume the ring independently: each waits on a stage's full barrier, copies its
+    // vectors to registers and releases the stage; the last warp to release it issues the next
+    // copy into it. The CTA meets only at checkpoints (every NSTAGE chunks and after the last),
+    // where it agrees on timeouts, candidate overflow and crowded slots (then compacts).
+    auto issue = [&](int64_t c) {
+      const int st = (int)(c % NSTAGE);
       const uint64_t pol = keep_in_l2 ? l2_policy_evict_last() : l2_policy_evict_first();
-      for (int c = 0; c < NSTAGE && c < nchunks; ++c) {
-        const int64_t nv = min((int64_t)CHUNK_VEC, s.nvec - (int64_t)c * CHUNK_VEC);
-        mbar_expect_tx(&sh.mbar[c], (uint32_t)(nv * 16));
-        bulk_load(ring + c * CHUNK_VEC, src + (int64_t)c * CHUNK_VEC, (uint32_t)(nv * 16), &sh.mbar[c], pol);
-      }
+      const int64_t nv = min((int64_t)CHUNK_VEC, s.nvec - c * CHUNK_VEC);
+      sh.stage_chunk[st] = c;
+      mbar_expect_tx(&sh.mbar[st], (uint32_t)(nv * 16));
+      bulk_load(ring + st * CHUNK_VEC, src + c * CHUNK_VEC, (uint32_t)(nv * 16), &sh.mbar[st], pol);
+    };
+    if (tid == 0)
+      for (int64_t c = 0; c < NSTAGE && c < nchunks; ++c) issue(c);
+    const int lane = tid & 31;
+    bool timed_out = false;  // this warp gave up waiting (warp-uniform)
+    if (filtering && nchunks > 0) {
+      // first threshold from the first chunk (it stays staged for the loop below)
+      timed_out = !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sh.mbar[0], 0u, WAIT_POLLS));
+      const int nv0 = (int)min((int64_t)CHUNK_VEC, s.nvec);
+      if (nv0 * EPV >= top_k) first_threshold<T, VPT>(ring, nv0, top_k, tf, sh);
     }
-    bool have_thr = !filtering;
-    for (int64_t c = 0; c < nchunks; ++c) {
-      const int stage = (int)(c % NSTAGE);
+    bool cta_timeout = false;
+    int cp = 0;              // checkpoints passed
+    // 32-bit chunk and vector counters: a slice holds fewer than 2^24 elements
+    const int nch = (int)nchunks, nvec32 = (int)s.nvec;
+    const uint32_t e_base = (uint32_t)s.vec_e0 + (uint32_t)tid * EPV;  // element of vector tid of chunk 0
+    float t = sh.thr_f;  // candidate threshold; changes only at checkpoints
+    for (int c = 0; c < nch; ++c) {
+      const int stage = c % NSTAGE;
       const uint32_t parity = (uint32_t)((c / NSTAGE) & 1);
-      if (!mbar_wait_bounded(&sh.mbar[stage], parity, WAIT_POLLS)) sh.timeout = 1;
-      __syncthreads();
-      if (sh.timeout) break;
-      const int nv = (int)min((int64_t)CHUNK_VEC, s.nvec - c * CHUNK_VEC);
+      if (!timed_out) timed_out = !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sh.mbar[stage], parity, WAIT_POLLS));
+      const int nv = min(CHUNK_VEC, nvec32 - c * CHUNK_VEC);
       const uint4* buf = ring + stage * CHUNK_VEC;
       // load every vector of this thread first (independent shared loads), then reduce
       float x[VPT][EPV];
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * NT + tid;
-        if (v < nv) {
+        if (v < nv && !timed_out) {
           Elem<T>::unpack(buf[v], x[j]);
         } else {
 #pragma unroll
           for (int q = 0; q < EPV; ++q) x[j][q] = -INFINITY;
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && !timed_out) {
+        // this warp is done with the stage; the last warp to release it refills it
+        if (atom_add_acq_rel(&sh.released[stage], 1u) == NW - 1) {
+          sh.released[stage] = 0;
+          if (c + NSTAGE < nch) {
+            fence_proxy_async();
+            issue(c + NSTAGE);
+          }
         }
       }
       float vm[VPT];
@@ -872,7 +946,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
 #pragma unroll
           for (int q = EPV - 1; q >= 0; --q)
             if (x[j][q] == vm[j]) jj = q;
-          bidx = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + j * NT + tid) * EPV) + jj;
+          bidx = e_base + (uint32_t)((c * CHUNK_VEC + j * NT) * EPV + jj);
         }
       }
       if (track_min) {
@@ -883,63 +957,50 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             if (x[j][q] > -INFINITY) mnv = fminf(mnv, x[j][q]);
       }
       if (filtering && !row_ovf) {
-        if (!have_thr) {
-          // exact first threshold: the k-th largest value of this first chunk
-          const int n0 = nv * EPV;
-          if (n0 >= top_k) {
-            uint32_t kk[VPT * EPV];
-            uint32_t mn = 0xFFFFFFFFu, mx = 0;
-#pragma unroll
-            for (int j = 0; j < VPT; ++j)
-#pragma unroll
-              for (int q = 0; q < EPV; ++q) {
-                const bool ok = j * NT + tid < nv;
-                kk[j * EPV + q] = ok ? key_of(x[j][q]) : 0u;
-                if (ok) mn = min(mn, kk[j * EPV + q]);
-                mx = max(mx, kk[j * EPV + q]);
-              }
-            uint32_t unused, kmin, kmax;
-            block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
-            const uint32_t k0 = block_kth_select<VPT * EPV>(kk, (uint32_t)top_k, kmin, (uint32_t)n0,
-                                                            (uint64_t)kmax + 1, false, sh);
-            if (tid == 0) sh.thr_f = tie_floor(value_of(k0), tf);
-          }
-          __syncthreads();
-          have_thr = true;
-        }
-        const float t = sh.thr_f;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
           if (j * NT + tid < nv && vm[j] >= t) {  // vectors past the chunk's end hold -inf padding
-            const uint32_t e0 = (uint32_t)(s.vec_e0 + (c * CHUNK_VEC + j * NT + tid) * EPV);
+            const uint32_t e0 = e_base + (uint32_t)((c * CHUNK_VEC + j * NT) * EPV);
 #pragma unroll
             for (int q = 0; q < EPV; ++q)
               if (x[j][q] >= t) push(x[j][q], e0 + q);
           }
         }
       }
-      // every thread is done with this stage: refill it, then compact if a thread's slots are half full
-      const int crowded = __syncthreads_or(filtering && nc >= SLOTS / 2);
-      if (tid == 0 && c + NSTAGE < nchunks) {
-        const uint64_t pol = keep_in_l2 ? l2_policy_evict_last() : l2_policy_evict_first();
-        const int64_t cn = c + NSTAGE;
-        const int64_t nv2 = min((int64_t)CHUNK_VEC, s.nvec - cn * CHUNK_VEC);
-        fence_proxy_async();
-        mbar_expect_tx(&sh.mbar[stage], (uint32_t)(nv2 * 16));
-        bulk_load(ring + stage * CHUNK_VEC, src + cn * CHUNK_VEC, (uint32_t)(nv2 * 16), &sh.mbar[stage], pol);
-      }
-      if (filtering) {
-        if (__syncthreads_or(ovf)) row_ovf = true;
-        if (crowded && !row_ovf) compact(top_k);
+      if (c % NSTAGE == NSTAGE - 1 || c == nch - 1) {
+        // checkpoint; flag and count words rotate over three slots so a reset never races a write
+        const int mine = (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && nc >= SLOTS / 2) ? 1 : 0);
+        if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
+        if (filtering) {
+          const uint32_t wsum = __reduce_add_sync(0xFFFFFFFFu, (uint32_t)nc);
+          if (lane == 0 && wsum) atomicAdd(&sh.cp_count[cp % 3], wsum);
+        }
+        __syncthreads();
+        const int f = sh.cp_flags[cp % 3];
+        const uint32_t held = sh.cp_count[cp % 3];
+        if (tid == 0) {
+          sh.cp_flags[(cp + 2) % 3] = 0;
+          sh.cp_count[(cp + 2) % 3] = 0;
+        }
+        ++cp;
+        if (f & 4) {
+          cta_timeout = true;
+          break;
+        }
+        if (f & 2) row_ovf = true;
+        // raise the threshold once the CTA holds a few times k candidates, so it keeps tracking
+        // the k-th of everything seen (the pass rate then falls with the chunks streamed)
+        if (((f & 1) || held >= (uint32_t)(4 * top_k + 64)) && !row_ovf) compact(top_k);
+        t = sh.thr_f;  // every thread passed the barrier after any write of the threshold
       }
     }
-    if (sh.timeout) {
+    if (cta_timeout) {
       // let every issued copy land before the shared memory is reused
       if (tid == 0) {
+        sh.timeout = 1;
         for (int st = 0; st < NSTAGE; ++st) {
-          int64_t last = -1;
-          for (int64_t c = st; c < nchunks; c += NSTAGE) last = c;
-          if (last >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((last / NSTAGE) & 1), WAIT_POLLS);
+          const int64_t c = sh.stage_chunk[st];
+          if (c >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((c / NSTAGE) & 1), WAIT_POLLS);
         }
       }
       __syncthreads();
