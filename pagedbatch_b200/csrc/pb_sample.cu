@@ -43,6 +43,7 @@ constexpr int RING_BYTES = 65536;
 constexpr int MAX_STAGE = 16;
 constexpr int CAND_CAP = 4096;      // candidate entries per CTA
 constexpr int SLOTS = CAND_CAP / NT; // candidate slots per thread
+constexpr int CP_CHUNKS = 8;        // chunks between CTA checkpoints (a multiple of the ring depth)
 constexpr uint32_t BUCKET = 32;     // keys left between the bisection bounds when it stops early
 constexpr int KSMALL = 1024;        // largest top_k resolved from the streamed candidates
 constexpr int KCAP = 2048;          // survivors of the small path sorted in rank 0
@@ -666,12 +667,16 @@ __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank,
 
 // First candidate threshold: sh.thr_f = the tie floor of the top_k-th largest value among the nv
 // staged vectors at buf (thread t owns vectors t, t + NT, ...). All threads call.
+// First candidate threshold, a lower bound of the row's top_k-th value taken from the nv staged
+// vectors at buf (thread t owns vectors t, t + NT, ...): the top_k-th largest per-thread maximum
+// when at least top_k threads hold values (every maximum is a value of the row), else the
+// top_k-th largest value. sh.thr_f = its tie floor. All threads call.
 template <typename T, int VPT>
 __device__ __noinline__ void first_threshold(const uint4* buf, int nv, int top_k, float tf, Shared& sh) {
   constexpr int EPV = Elem<T>::EPV;
   const int tid = threadIdx.x;
   uint32_t kk[VPT * EPV];
-  uint32_t mn = 0xFFFFFFFFu, mx = 0;
+  uint32_t mn = 0xFFFFFFFFu, mx = 0, tmax = 0;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const bool ok = j * NT + tid < nv;
@@ -684,10 +689,19 @@ __device__ __noinline__ void first_threshold(const uint4* buf, int nv, int top_k
       mx = max(mx, kk[j * EPV + q]);
     }
   }
-  uint32_t unused, kmin, kmax;
-  block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
-  const uint32_t k0 = block_kth_select<VPT * EPV>(kk, (uint32_t)top_k, kmin, (uint32_t)(nv * EPV), (uint64_t)kmax + 1,
-                                                  false, sh);
+  tmax = mx;  // this thread's maximum key (0 if it holds no value)
+  const int holders = min(nv, NT);
+  uint32_t k0;
+  if (holders >= top_k) {
+    uint32_t one[1] = {tmax};
+    uint32_t unused, tmin, tmx;
+    block_sum_min_max(0u, tmax ? tmax : 0xFFFFFFFFu, tmax, sh, &unused, &tmin, &tmx);
+    k0 = block_kth_select<1>(one, (uint32_t)top_k, tmin, (uint32_t)holders, (uint64_t)tmx + 1, false, sh);
+  } else {
+    uint32_t unused, kmin, kmax;
+    block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+    k0 = block_kth_select<VPT * EPV>(kk, (uint32_t)top_k, kmin, (uint32_t)(nv * EPV), (uint64_t)kmax + 1, false, sh);
+  }
   if (tid == 0) sh.thr_f = tie_floor(value_of(k0), tf);
   __syncthreads();
 }
@@ -938,15 +952,18 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         vm[j] = a;
       }
 #pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        runmax = fmax_nan(runmax, vm[j]);
-        if (vm[j] > bestv) {
-          bestv = vm[j];
-          int jj = EPV - 1;
+      for (int j = 0; j < VPT; ++j) runmax = fmax_nan(runmax, vm[j]);
+      if (greedy) {  // only greedy rows need the index of the first maximum
 #pragma unroll
-          for (int q = EPV - 1; q >= 0; --q)
-            if (x[j][q] == vm[j]) jj = q;
-          bidx = e_base + (uint32_t)((c * CHUNK_VEC + j * NT) * EPV + jj);
+        for (int j = 0; j < VPT; ++j) {
+          if (vm[j] > bestv) {
+            bestv = vm[j];
+            int jj = EPV - 1;
+#pragma unroll
+            for (int q = EPV - 1; q >= 0; --q)
+              if (x[j][q] == vm[j]) jj = q;
+            bidx = e_base + (uint32_t)((c * CHUNK_VEC + j * NT) * EPV + jj);
+          }
         }
       }
       if (track_min) {
@@ -967,7 +984,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           }
         }
       }
-      if (c % NSTAGE == NSTAGE - 1 || c == nch - 1) {
+      if (c % CP_CHUNKS == CP_CHUNKS - 1 || c == nch - 1) {
         // checkpoint; flag and count words rotate over three slots so a reset never races a write
         const int mine = (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && nc >= SLOTS / 2) ? 1 : 0);
         if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
