@@ -113,6 +113,20 @@ PB_API int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t voca
                      pb_row_info* out_info, float* out_probs, void* stream);
 
 /*
+ * The same sampler as three stream-ordered launches over a caller-provided workspace: a lean
+ * slice scan (greedy rows and top-k rows with k <= 512; 4 CTAs per SM), the merge of the slices'
+ * candidate records (as pb_merge), and pb_sample's full-row kernel restricted to the rows the first
+ * two could not settle. Results are identical to pb_sample. Replaces the same call as pb_sample
+ * (pagedbatch/sampling.py:10-27). With out_probs it runs pb_sample itself. workspace: device
+ * memory of at least pb_sample_ws_bytes(n_rows, vocab, dtype) bytes, 256-byte aligned, not used by
+ * another call while this one runs.
+ */
+PB_API int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype);
+PB_API int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                        const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
+                        pb_row_info* out_info, float* out_probs, void* workspace, int64_t ws_bytes, void* stream);
+
+/*
  * Vocabulary-parallel sampling (rows split by columns over N shards, as the output of a
  * tensor-parallel LM head). No counterpart in the reference, which samples whole rows; the result
  * is the same as pb_sample on the full rows: the union of every shard's top-k survivors (all

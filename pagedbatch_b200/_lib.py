@@ -49,8 +49,8 @@ def record_bytes(cap: int) -> int:
     """Bytes of one row's candidate record (pb_record_bytes)."""
     return CAND_HEADER.itemsize + 8 * int(cap)
 
-EXPORTS = ("pb_sample", "pb_candidates", "pb_merge", "pb_record_bytes", "pb_key_of", "pb_exp", "pb_strerror",
-           "pb_version")
+EXPORTS = ("pb_sample", "pb_sample_ws", "pb_sample_ws_bytes", "pb_candidates", "pb_merge", "pb_record_bytes",
+           "pb_key_of", "pb_exp", "pb_strerror", "pb_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -77,6 +77,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
     L.pb_sample.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp]
     L.pb_sample.restype = i32
+    L.pb_sample_ws.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp, i64, vp]
+    L.pb_sample_ws.restype = i32
+    L.pb_sample_ws_bytes.argtypes = [i64, i64, i32]
+    L.pb_sample_ws_bytes.restype = i64
     L.pb_candidates.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, i32, vp, vp]
     L.pb_candidates.restype = i32
     L.pb_merge.argtypes = [vp, i32, i64, i32, vp, vp, vp, vp]

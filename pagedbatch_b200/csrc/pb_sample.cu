@@ -68,6 +68,7 @@ struct Args {
   int64_t* out_token;
   pb_row_info* out_info;
   float* out_probs;
+  const pb_row_info* only_fallback;  // if set: sample only the rows whose status there is PB_ROW_FALLBACK
   uint8_t* cand_out;     // vocabulary-parallel shard mode: per-row candidate records (else null)
   int32_t cand_cap;      // entries per record
   int64_t vocab_offset;  // global index of this shard's first column
@@ -805,6 +806,8 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   const int64_t item = blockIdx.x / C;
   const int tid = threadIdx.x;
   const int64_t V = a.vocab;
+  // rows another launch already settled: every CTA of the cluster leaves before any cluster step
+  if (a.only_fallback && a.only_fallback[item].status != PB_ROW_FALLBACK) return;
 
   if (tid == 0) {
     const pb_row_params p = a.params[item];
@@ -1865,6 +1868,321 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
   }
 }
 
+// ---- slice scan: the lean streaming stage of the three-launch path ----------------------------
+//
+// pb_sample_ws runs a batch as scan_kernel (one CTA per row slice, no clusters, 48 KB of shared
+// memory and at most 64 registers, so 4 CTAs share an SM) -> merge_kernel (one CTA per row) ->
+// sample_kernel restricted to the rows the merge could not settle. The scan handles greedy rows and
+// top-k rows with k <= L_KMAX and writes the vocabulary-parallel record format: a slice is a shard.
+
+constexpr int L_CHUNK_BYTES = 8192;                 // bytes per staged chunk
+constexpr int L_NSTAGE = 4;                         // ring depth
+constexpr int L_RING = L_CHUNK_BYTES * L_NSTAGE;    // 32 KB
+constexpr int L_SLOTS = 8;                          // candidate slots per thread
+constexpr int L_SMEM = L_RING + L_SLOTS * NT * 8;   // 48 KB
+constexpr int L_CAP = 1024;                         // entries per slice record
+constexpr int L_KMAX = 512;                         // largest top_k the scan resolves
+constexpr int L_CP_CHUNKS = 8;                      // chunks between CTA checkpoints
+static_assert(L_SLOTS <= SLOTS, "compact_slots walks at most SLOTS slots");
+static_assert(L_NSTAGE <= MAX_STAGE, "ring barriers live in Shared");
+
+struct ScanArgs {
+  const char* logits;
+  int64_t n_rows, vocab, row_stride;
+  const int32_t* row_index;
+  const pb_row_params* params;
+  int32_t slices;
+  uint8_t* records;  // [slices][n_rows][record_bytes(L_CAP)]
+};
+
+template <typename T>
+__global__ void __launch_bounds__(NT, 4) scan_kernel(ScanArgs a) {
+  constexpr int EPV = Elem<T>::EPV;
+  constexpr int CV = L_CHUNK_BYTES / 16;  // vectors per chunk
+  constexpr int VPT = CV / NT;            // vectors per thread per chunk
+  static_assert(CV % NT == 0, "chunk must split evenly");
+  extern __shared__ __align__(128) unsigned char dyn[];
+  __shared__ Shared sh;
+  uint4* ring = reinterpret_cast<uint4*>(dyn);
+  uint64_t* slots = reinterpret_cast<uint64_t*>(dyn + L_RING);
+  const int S = a.slices;
+  const int64_t item = blockIdx.x / S;
+  const int rank = (int)(blockIdx.x % S);
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t V = a.vocab;
+  uint8_t* rec = a.records + ((int64_t)rank * a.n_rows + item) * record_bytes(L_CAP);
+  pb_cand_header* hdr = reinterpret_cast<pb_cand_header*>(rec);
+  uint64_t* ent = reinterpret_cast<uint64_t*>(rec + sizeof(pb_cand_header));
+
+  const pb_row_params p = a.params[item];
+  const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
+  const bool greedy = !bad && p.temperature == 0.0;
+  const bool filtering = !bad && !greedy && p.top_k > 0 && (int64_t)p.top_k < V && p.top_k <= L_KMAX;
+  if (!greedy && !filtering) {
+    // rejected parameters are settled by the merge; every other row needs the full-row sampler
+    if (tid == 0) {
+      hdr->count = 0;
+      hdr->flags = bad ? PB_ROW_BAD_PARAMS : PB_CAND_FALLBACK;
+      hdr->max_key = 0.0f;
+      hdr->reserved = 0;
+    }
+    return;
+  }
+  const float tf = (float)p.temperature;
+  const int32_t top_k = p.top_k;
+  const int64_t row_id = a.row_index ? (int64_t)a.row_index[item] : item;
+  const T* row = reinterpret_cast<const T*>(a.logits) + row_id * a.row_stride;
+  const Slice s = make_slice(row, V, rank, S);
+  if (tid == 0) {
+    for (int st = 0; st < L_NSTAGE; ++st) {
+      mbar_init(&sh.mbar[st], 1);
+      sh.stage_chunk[st] = -1;
+      sh.released[st] = 0;
+    }
+    sh.cp_flags[0] = sh.cp_flags[1] = sh.cp_flags[2] = 0;
+    sh.cp_count[0] = sh.cp_count[1] = sh.cp_count[2] = 0;
+    sh.thr_f = -INFINITY;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  float runmax = -INFINITY, bestv = -INFINITY;
+  uint32_t bidx = 0xFFFFFFFFu;
+  int nc = 0;
+  bool ovf = false, row_ovf = false;
+  auto push = [&](float x, uint32_t e) {
+    if (nc < L_SLOTS) {
+      slots[nc * NT + tid] = compose(key_of(x), e);
+      ++nc;
+    } else {
+      ovf = true;
+    }
+  };
+  for (int64_t e = tid; e < s.head_n; e += NT) {
+    const float x = Elem<T>::ld(row + e);
+    runmax = fmax_nan(runmax, x);
+    if (greedy && x > bestv) {
+      bestv = x;
+      bidx = (uint32_t)e;
+    }
+  }
+  const int nch = (int)((s.nvec + CV - 1) / CV), nvec32 = (int)s.nvec;
+  const uint4* src = reinterpret_cast<const uint4*>(row + s.vec_e0);
+  auto issue = [&](int c) {
+    const int st = c % L_NSTAGE;
+    const int nv = min(CV, nvec32 - c * CV);
+    sh.stage_chunk[st] = c;
+    mbar_expect_tx(&sh.mbar[st], (uint32_t)(nv * 16));
+    bulk_load(ring + st * CV, src + (int64_t)c * CV, (uint32_t)(nv * 16), &sh.mbar[st], l2_policy_evict_first());
+  };
+  if (tid == 0)
+    for (int c = 0; c < L_NSTAGE && c < nch; ++c) issue(c);
+  bool timed_out = false, cta_timeout = false;
+  if (filtering && nch > 0) {
+    // first threshold from the first chunk (it stays staged for the loop below)
+    timed_out = !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sh.mbar[0], 0u, WAIT_POLLS));
+    const int nv0 = min(CV, nvec32);
+    if (nv0 * EPV >= top_k) first_threshold<T, VPT>(ring, nv0, top_k, tf, sh);
+  }
+  float t = sh.thr_f;
+  const uint32_t e_base = (uint32_t)s.vec_e0 + (uint32_t)tid * EPV;
+  int cp = 0;
+  for (int c = 0; c < nch; ++c) {
+    const int stage = c % L_NSTAGE;
+    if (!timed_out)
+      timed_out = !__all_sync(0xFFFFFFFFu,
+                              mbar_wait_bounded(&sh.mbar[stage], (uint32_t)((c / L_NSTAGE) & 1), WAIT_POLLS));
+    const int nv = min(CV, nvec32 - c * CV);
+    const uint4* buf = ring + stage * CV;
+    float x[VPT][EPV];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = j * NT + tid;
+      if (v < nv && !timed_out) {
+        Elem<T>::unpack(buf[v], x[j]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) x[j][q] = -INFINITY;
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && !timed_out) {
+      // this warp is done with the stage; the last warp to release it refills it
+      if (atom_add_acq_rel(&sh.released[stage], 1u) == NW - 1) {
+        sh.released[stage] = 0;
+        if (c + L_NSTAGE < nch) {
+          fence_proxy_async();
+          issue(c + L_NSTAGE);
+        }
+      }
+    }
+    float vm[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      float m2 = fmax_nan(x[j][0], x[j][1]);
+#pragma unroll
+      for (int q = 2; q < EPV; ++q) m2 = fmax_nan(m2, x[j][q]);
+      vm[j] = m2;
+      runmax = fmax_nan(runmax, m2);
+    }
+    if (greedy) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        if (vm[j] > bestv) {
+          bestv = vm[j];
+          int jj = EPV - 1;
+#pragma unroll
+          for (int q = EPV - 1; q >= 0; --q)
+            if (x[j][q] == vm[j]) jj = q;
+          bidx = e_base + (uint32_t)((c * CV + j * NT) * EPV + jj);
+        }
+      }
+    } else if (!row_ovf) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        if (j * NT + tid < nv && vm[j] >= t) {  // vectors past the chunk's end hold -inf padding
+          const uint32_t e0 = e_base + (uint32_t)((c * CV + j * NT) * EPV);
+#pragma unroll
+          for (int q = 0; q < EPV; ++q)
+            if (x[j][q] >= t) push(x[j][q], e0 + q);
+        }
+      }
+    }
+    if (c % L_CP_CHUNKS == L_CP_CHUNKS - 1 || c == nch - 1) {
+      // checkpoint; flag and count words rotate over three slots so a reset never races a write
+      const int mine = (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && nc >= L_SLOTS / 2) ? 1 : 0);
+      if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
+      if (filtering) {
+        const uint32_t wsum = __reduce_add_sync(0xFFFFFFFFu, (uint32_t)nc);
+        if (lane == 0 && wsum) atomicAdd(&sh.cp_count[cp % 3], wsum);
+      }
+      __syncthreads();
+      const int f = sh.cp_flags[cp % 3];
+      const uint32_t held = sh.cp_count[cp % 3];
+      if (tid == 0) {
+        sh.cp_flags[(cp + 2) % 3] = 0;
+        sh.cp_count[(cp + 2) % 3] = 0;
+      }
+      ++cp;
+      if (f & 4) {
+        cta_timeout = true;
+        break;
+      }
+      if (f & 2) row_ovf = true;
+      if (((f & 1) || held >= (uint32_t)(4 * top_k + 64)) && !row_ovf) nc = compact_slots(slots, nc, top_k, tf, sh);
+      t = sh.thr_f;  // every thread passed the barrier after any write of the threshold
+    }
+  }
+  if (cta_timeout) {
+    // let every issued copy land before the block leaves
+    if (tid == 0)
+      for (int st = 0; st < L_NSTAGE; ++st) {
+        const int64_t c = sh.stage_chunk[st];
+        if (c >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((c / L_NSTAGE) & 1), WAIT_POLLS);
+      }
+    __syncthreads();
+    if (tid == 0) {
+      hdr->count = 0;
+      hdr->flags = PB_ROW_TIMEOUT;
+      hdr->max_key = 0.0f;
+      hdr->reserved = 0;
+    }
+    return;
+  }
+  for (int64_t e = tid; e < s.tail_n; e += NT) {
+    const float x = Elem<T>::ld(row + s.tail_e0 + e);
+    runmax = fmax_nan(runmax, x);
+    if (greedy && x > bestv) {
+      bestv = x;
+      bidx = (uint32_t)(s.tail_e0 + e);
+    }
+  }
+  if (filtering) {
+    // head and tail elements against the final threshold
+    for (int64_t e = tid; e < s.head_n; e += NT) {
+      const float x = Elem<T>::ld(row + e);
+      if (x >= t) push(x, (uint32_t)e);
+    }
+    for (int64_t e = tid; e < s.tail_n; e += NT) {
+      const float x = Elem<T>::ld(row + s.tail_e0 + e);
+      if (x >= t) push(x, (uint32_t)(s.tail_e0 + e));
+    }
+    if (__syncthreads_or(ovf)) row_ovf = true;
+  }
+  // CTA reduction: NaN-propagating max, first maximum (greedy)
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bestv, o);
+    const uint32_t i2 = __shfl_xor_sync(0xFFFFFFFFu, bidx, o);
+    if (v2 > bestv || (v2 == bestv && i2 < bidx)) {
+      bestv = v2;
+      bidx = i2;
+    }
+    runmax = fmax_nan(runmax, __shfl_xor_sync(0xFFFFFFFFu, runmax, o));
+  }
+  __shared__ float lwf[NW], lwm[NW];
+  __shared__ uint32_t lwi[NW];
+  if (lane == 0) {
+    lwf[tid >> 5] = bestv;
+    lwi[tid >> 5] = bidx;
+    lwm[tid >> 5] = runmax;
+  }
+  __syncthreads();
+  for (int w = 0; w < NW; ++w) {
+    if (lwf[w] > bestv || (lwf[w] == bestv && lwi[w] < bidx)) {
+      bestv = lwf[w];
+      bidx = lwi[w];
+    }
+    runmax = fmax_nan(runmax, lwm[w]);
+  }
+  if (greedy) {
+    if (tid == 0) {
+      int32_t count = 0, flags = PB_CAND_GREEDY;
+      if (runmax != runmax) {
+        flags = PB_CAND_FALLBACK;  // a NaN: the full-row sampler finds the first one
+      } else if (s.e_hi > s.e_lo) {
+        // every value -inf: the slice's first index stands for its maximum
+        ent[0] = compose(key_of(bestv), (bidx == 0xFFFFFFFFu) ? (uint32_t)s.e_lo : bidx);
+        count = 1;
+      }
+      hdr->count = count;
+      hdr->flags = flags;
+      hdr->max_key = bestv;
+      hdr->reserved = 0;
+    }
+    return;
+  }
+  const float m = __fdiv_rn(runmax, tf);
+  const uint32_t mk = key_of(m);
+  int32_t flags = 0;
+  if (mk >= KEY_POS_INF) flags = PB_ROW_NONFINITE;                  // NaN or +inf: so is the whole row
+  else if (mk <= KEY_NEG_INF || row_ovf) flags = PB_CAND_FALLBACK;  // all -inf here, or too many ties
+  if (flags) {
+    if (tid == 0) {
+      hdr->count = 0;
+      hdr->flags = flags;
+      hdr->max_key = m;
+      hdr->reserved = 0;
+    }
+    return;
+  }
+  // shrink to (about) this slice's top_k, then publish with scaled keys and global indices
+  nc = compact_slots(slots, nc, top_k, tf, sh);
+  uint32_t tot;
+  const uint32_t pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
+  if (tot <= (uint32_t)L_CAP) {
+    for (int j = 0; j < nc; ++j) {
+      const uint64_t cv = slots[j * NT + tid];
+      ent[pos + j] = compose(key_of(__fdiv_rn(value_of(comp_key(cv)), tf)), comp_idx(cv));
+    }
+  }
+  if (tid == 0) {
+    hdr->count = (tot <= (uint32_t)L_CAP) ? (int32_t)tot : 0;
+    hdr->flags = (tot <= (uint32_t)L_CAP) ? 0 : PB_CAND_FALLBACK;
+    hdr->max_key = m;
+    hdr->reserved = 0;
+  }
+}
+
 template <typename T>
 int launch(const Args& a, int C, cudaStream_t stream) {
   // the dynamic shared memory limit is a per-device function attribute
@@ -1916,6 +2234,114 @@ int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
   return C;
 }
 
+
+int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,
+                 int64_t* out_token, pb_row_info* out_info, cudaStream_t stream) {
+  static unsigned long long configured = 0;  // bit d: device d configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_SMEM) != cudaSuccess)
+      return PB_E_DEVICE;
+    configured |= 1ull << dev;
+  }
+  MergeArgs m;
+  m.records = records;
+  m.n_shards = n_shards;
+  m.n_rows = n_rows;
+  m.cap = cap;
+  m.params = params;
+  m.out_token = out_token;
+  m.out_info = out_info;
+  merge_kernel<<<(unsigned)n_rows, NT, MERGE_SMEM, stream>>>(m);
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  return PB_OK;
+}
+
+template <typename T>
+int launch_scan(const ScanArgs& a, cudaStream_t stream) {
+  static unsigned long long configured = 0;  // bit d: device d configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, L_SMEM) != cudaSuccess)
+      return PB_E_DEVICE;
+    configured |= 1ull << dev;
+  }
+  scan_kernel<T><<<(unsigned)(a.n_rows * a.slices), NT, L_SMEM, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  return PB_OK;
+}
+
+// Slices per row for the scan: about four CTAs per SM over the batch, slices of at least 32 KB.
+int slices_for(int64_t n_rows, int64_t vocab, int es) {
+  const char* env = getenv("PB_SLICES");
+  if (env) {
+    const int c = atoi(env);
+    if (c == 1 || c == 2 || c == 4 || c == 8) return c;
+  }
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  const int64_t want = 4 * (int64_t)sms[dev];
+  const int64_t bytes = vocab * es;
+  int S = 1;
+  while (S < 8 && n_rows * 2 * S <= want && bytes / (2 * S) >= 32768) S <<= 1;
+  return S;
+}
+
+// workspace of pb_sample_ws: the slices' records, then the merge's per-row info
+int64_t ws_bytes_for(int64_t n_rows, int S) {
+  return (int64_t)S * n_rows * record_bytes(L_CAP) + n_rows * (int64_t)sizeof(pb_row_info);
+}
+
+// scan -> merge -> full-row kernel on the rows the merge left as PB_ROW_FALLBACK (see pb_sample_ws)
+int run_split(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
+              const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
+              uint8_t* workspace, int S, cudaStream_t st) {
+  uint8_t* records = workspace;
+  pb_row_info* info =
+      out_info ? out_info : reinterpret_cast<pb_row_info*>(records + (int64_t)S * n_rows * record_bytes(L_CAP));
+  ScanArgs sa;
+  sa.logits = static_cast<const char*>(logits);
+  sa.n_rows = n_rows;
+  sa.vocab = vocab;
+  sa.row_stride = row_stride;
+  sa.row_index = row_index;
+  sa.params = params;
+  sa.slices = S;
+  sa.records = records;
+  int rc = (dtype == PB_DTYPE_F32)    ? launch_scan<float>(sa, st)
+           : (dtype == PB_DTYPE_BF16) ? launch_scan<__nv_bfloat16>(sa, st)
+                                      : launch_scan<__half>(sa, st);
+  if (rc != PB_OK) return rc;
+  rc = launch_merge(records, S, n_rows, L_CAP, params, out_token, info, st);
+  if (rc != PB_OK) return rc;
+  Args a;
+  a.logits = static_cast<const char*>(logits);
+  a.n_rows = n_rows;
+  a.vocab = vocab;
+  a.row_stride = row_stride;
+  a.row_index = row_index;
+  a.params = params;
+  a.out_token = out_token;
+  a.out_info = out_info;
+  a.out_probs = nullptr;
+  a.only_fallback = info;
+  a.cand_out = nullptr;
+  a.cand_cap = 0;
+  a.vocab_offset = 0;
+  const int C = cluster_size_for(n_rows, vocab, es);
+  if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
+  if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
+  return launch<__half>(a, C, st);
+}
 }  // namespace
 
 extern "C" {
@@ -1941,6 +2367,7 @@ int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int6
   a.out_token = out_token;
   a.out_info = out_info;
   a.out_probs = out_probs;
+  a.only_fallback = nullptr;
   a.cand_out = nullptr;
   a.cand_cap = 0;
   a.vocab_offset = 0;
@@ -1976,6 +2403,7 @@ int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t shard_v
   a.out_token = nullptr;
   a.out_info = nullptr;
   a.out_probs = nullptr;
+  a.only_fallback = nullptr;
   a.cand_out = static_cast<uint8_t*>(out_records);
   a.cand_cap = cap;
   a.vocab_offset = vocab_offset;
@@ -1993,25 +2421,35 @@ int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap,
   if (!records || !params || !out_token) return PB_E_INVALID;
   if (n_rows > (int64_t)0x7FFFFFFF) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(records) & 15) != 0) return PB_E_INVALID;
-  static unsigned long long configured = 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
-  if (!(configured & (1ull << dev))) {
-    if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_SMEM) != cudaSuccess)
-      return PB_E_DEVICE;
-    configured |= 1ull << dev;
-  }
-  MergeArgs m;
-  m.records = static_cast<const uint8_t*>(records);
-  m.n_shards = n_shards;
-  m.n_rows = n_rows;
-  m.cap = cap;
-  m.params = params;
-  m.out_token = out_token;
-  m.out_info = out_info;
-  merge_kernel<<<(unsigned)n_rows, NT, MERGE_SMEM, static_cast<cudaStream_t>(stream)>>>(m);
-  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
-  return PB_OK;
+  return launch_merge(static_cast<const uint8_t*>(records), n_shards, n_rows, cap, params, out_token, out_info,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype) {
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
+  return ws_bytes_for(n_rows, slices_for(n_rows, vocab, es));
+}
+
+int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                 const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
+                 float* out_probs, void* workspace, int64_t ws_bytes, void* stream) {
+  if (out_probs)  // probabilities come from the full-row path
+    return pb_sample(logits, dtype, n_rows, vocab, row_stride, row_index, params, out_token, out_info, out_probs,
+                     stream);
+  if (n_rows < 0 || vocab <= 0 || row_stride < vocab) return PB_E_INVALID;
+  if (vocab >= PB_MAX_VOCAB) return PB_E_TOO_LARGE;
+  if (n_rows == 0) return PB_OK;
+  if (!logits || !params || !out_token || !workspace) return PB_E_INVALID;
+  if (n_rows > (int64_t)(0x7FFFFFFF / 8)) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return PB_E_INVALID;
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  const int S = slices_for(n_rows, vocab, es);
+  if (ws_bytes < ws_bytes_for(n_rows, S)) return PB_E_INVALID;
+  return run_split(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
+                   static_cast<uint8_t*>(workspace), S, static_cast<cudaStream_t>(stream));
 }
 
 uint32_t pb_key_of(float x) {

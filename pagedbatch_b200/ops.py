@@ -14,6 +14,7 @@ current CUDA stream of the logits' device, with no synchronisation.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 import torch
@@ -42,6 +43,29 @@ def params_tensor(rec: np.ndarray, device, pinned: bool = True) -> torch.Tensor:
     return host.to(device, non_blocking=True)
 
 
+_WS: dict = {}
+
+
+def _split_path() -> bool:
+    """The single full-row launch (default) or, with PB_PATH=split, scan + merge + fallback launches."""
+    return os.environ.get("PB_PATH", "full") == "split"
+
+
+def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device scratch for pb_sample_ws, grown on demand (torch allocations are 256-byte aligned).
+
+    Launches on one device are stream-ordered; a caller that samples on several streams of the same
+    device at once must not share this buffer."""
+    if nbytes < 0:
+        raise ValueError("bad workspace request")
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _WS[key] = ws
+    return ws
+
+
 def _launch(logits: torch.Tensor, params: torch.Tensor, row_index, with_info: bool, with_probs: bool,
             check_rows: bool = True):
     if not logits.is_cuda:
@@ -66,6 +90,19 @@ def _launch(logits: torch.Tensor, params: torch.Tensor, row_index, with_info: bo
     info = torch.empty((n, _lib.ROW_INFO.itemsize), dtype=torch.uint8, device=dev) if with_info else None
     probs = torch.empty((n, V), dtype=torch.float32, device=dev) if with_probs else None
     L = _lib.load()
+    if not with_probs and _split_path():
+        with torch.cuda.device(dev):
+            need = L.pb_sample_ws_bytes(n, V, _DTYPE_CODE[logits.dtype])
+            ws = _workspace(dev, need)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            rc = L.pb_sample_ws(
+                ctypes.c_void_p(logits.data_ptr()), _DTYPE_CODE[logits.dtype], n, V, logits.stride(0),
+                ctypes.c_void_p(row_index.data_ptr()) if row_index is not None else None,
+                ctypes.c_void_p(params.data_ptr()), ctypes.c_void_p(tokens.data_ptr()),
+                ctypes.c_void_p(info.data_ptr()) if info is not None else None, None,
+                ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(stream))
+        _lib.check(rc, "pb_sample_ws")
+        return tokens, info, probs
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = L.pb_sample(

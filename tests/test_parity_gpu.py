@@ -57,6 +57,8 @@ def rec_for(params, uniforms):
 def _need_cuda(cuda):
     yield
     os.environ.pop("PB_CLUSTER", None)
+    os.environ.pop("PB_SLICES", None)
+    os.environ.pop("PB_PATH", None)
 
 
 def test_golden_rows(golden):
@@ -298,3 +300,72 @@ def test_vocab_parallel_api_one_rank_nccl():
         assert a == b
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("slices", ["1", "2", "4", "8"])
+def test_split_path_modes_and_edges(slices):
+    """The scan + merge + fallback launches (pb_sample_ws) against the oracle, every slice count."""
+    os.environ["PB_PATH"] = "split"
+    os.environ["PB_SLICES"] = slices
+    rng = np.random.default_rng(20 + int(slices))
+    for V in (1, 3, 17, 258, 4099, 49152, 128256):
+        B = 24
+        x = workloads.head_boosted(B, V, seed=V)
+        t = rng.choice([0.0, 0.5, 0.7, 1.0, 1.5], B)
+        k = rng.choice([0, 1, 2, 20, 50, 512, 513, 1000, max(1, V - 1), V], B)
+        p = rng.choice([1.0, 0.5, 0.9, 0.99, 1e-6], B)
+        u = rng.random(B)
+        u[:2] = [0.0, np.nextafter(1.0, 0.0)]
+        compare(x, oracle.make_params(t, p, k, u), probs=False, label=f"split S={slices} V={V}")
+    x = torch.randn(7, 600)
+    x[0, 5] = float("nan")
+    x[1, 7] = float("inf")
+    x[2, :] = float("-inf")
+    x[3, 300:] = float("-inf")
+    x[4, :] = 1.0
+    x[6, 100:] = float("-inf")
+    rec = oracle.make_params([1.0, 1.0, 1.0, 1.0, 0.0, 1.0, 0.0], [1.0] * 7, [10, 10, 10, 10, 0, 10, 0], [0.5] * 7)
+    rec["uniform"][5] = 1.0
+    compare(x, rec, probs=False, label=f"split nonfinite S={slices}")
+    x2 = torch.tensor([[1.0, float("nan"), 3.0, float("nan")], [float("-inf")] * 4, [-0.0, 0.0, -1.0, 0.0]])
+    compare(x2, oracle.make_params([0.0] * 3, [1.0] * 3, [0] * 3, [0.0] * 3), probs=False, label="split greedy edge")
+    rec = oracle.make_params([-1.0, 1.0, 1.0, float("nan")], [1.0, 0.0, 1.5, 1.0], [0, 0, 0, 0], [0.5] * 4)
+    compare(torch.randn(4, 100), rec, probs=False, label="split bad params")
+
+
+def test_split_path_configs_and_row_index():
+    os.environ["PB_PATH"] = "split"
+    for w in (workloads.config0(), workloads.config1(), workloads.config2()):
+        compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label=f"split {w.name}")
+    w = workloads.config1(rows=32)
+    sel = np.array([31, 0, 5, 5, 17, 2, 30], np.int32)
+    rec = rec_for([w.params[i] for i in sel], [w.uniforms()[i] for i in sel])
+    compare(w.logits, rec, sel, probs=False, label="split row_index")
+    os.environ.pop("PB_PATH")
+    compare(w.logits, rec, sel, probs=False, label="full row_index")
+
+
+def test_split_path_ties_and_sparse_rows():
+    os.environ["PB_PATH"] = "split"
+    V = 20000
+    x = torch.zeros(6, V)
+    x[1, ::3] = 1.0
+    x[2] = torch.randint(0, 3, (V,), generator=torch.Generator().manual_seed(0)).float()
+    x[3, 100] = 5.0
+    x[4] = (torch.arange(V) % 7).float()
+    x[5, :] = -1.0
+    rng = np.random.default_rng(13)
+    for t, k, p in [(0.5, 500, 1.0), (1.0, 7, 0.99), (0.0, 0, 1.0), (1.0, 1, 1.0), (1.0, 300, 0.3)]:
+        for sl in ("1", "4"):
+            os.environ["PB_SLICES"] = sl
+            compare(x, oracle.make_params([t] * 6, [p] * 6, [k] * 6, rng.random(6)), probs=False,
+                    label=f"split ties t={t} k={k} S={sl}")
+    V = 4099
+    x = torch.full((4, V), float("-inf"))
+    for r, n in enumerate((1, 37, 500, 999)):
+        cols = torch.from_numpy(rng.choice(V, n, replace=False))
+        x[r, cols] = torch.randn(n, generator=torch.Generator().manual_seed(r)) * 2.0
+    rec = oracle.make_params([1.0, 0.7, 1.0, 1.3], [1.0, 0.9, 1.0, 0.5], [400, 400, 400, 400], rng.random(4))
+    for sl in ("1", "8"):
+        os.environ["PB_SLICES"] = sl
+        compare(x, rec, probs=False, label=f"split sparse-finite S={sl}")
