@@ -50,6 +50,7 @@ extern "C" {
 #define PB_E_TOO_LARGE (-2)  /* vocab >= PB_MAX_VOCAB */
 #define PB_E_LAUNCH (-3)     /* the CUDA launch failed (cudaGetLastError after the launch) */
 #define PB_E_DEVICE (-4)     /* no usable sm_100 device / attribute query failed */
+#define PB_E_SCRATCH (-5)    /* pb_sample_noalloc: the batch needs more than its fixed scratch */
 
 /* Largest vocabulary: sums of 2^40-scaled weights must fit in 64 bits. */
 #define PB_MAX_VOCAB (1 << 24)
@@ -125,6 +126,24 @@ PB_API int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype);
 PB_API int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
                         const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
                         pb_row_info* out_info, float* out_probs, void* workspace, int64_t ws_bytes, void* stream);
+
+/*
+ * pb_sample_ws for callers that cannot allocate device memory: no counterpart in the reference.
+ * Some callers own no allocator (a plugin inside an application that manages every byte of the
+ * GPU itself, or plain C code without cudaMalloc); this entry point allocates nothing and uses a
+ * fixed scratch array compiled into the library instead of a workspace. Every GPU that loads the
+ * library holds that array (pb_sample_noalloc_max_bytes(), 32 MiB) until the process exits.
+ * Same arguments and results as pb_sample_ws without out_probs (probabilities need pb_sample).
+ * A batch that needs more scratch than the array holds (about 4000 rows at one slice per row,
+ * fewer with more slices; pb_sample_ws_bytes gives the need) returns PB_E_SCRATCH and launches
+ * nothing. The first call on each device looks up the array's device address; make that call
+ * before any stream capture. All calls share the one array, so calls that overlap on the GPU
+ * (two streams, or two host threads) race and corrupt each other's results; keep them ordered.
+ */
+PB_API int64_t pb_sample_noalloc_max_bytes(void);
+PB_API int pb_sample_noalloc(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                             const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
+                             pb_row_info* out_info, void* stream);
 
 /*
  * Vocabulary-parallel sampling (rows split by columns over N shards, as the output of a

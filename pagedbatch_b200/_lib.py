@@ -16,7 +16,8 @@ LIB_PATH = os.path.join(PKG, "_pb_sample.so")
 
 PB_DTYPE = {"float32": 0, "bfloat16": 1, "float16": 2}
 PB_OK = 0
-ERRORS = {-1: "invalid argument", -2: "vocabulary too large", -3: "kernel launch failed", -4: "device configuration failed"}
+ERRORS = {-1: "invalid argument", -2: "vocabulary too large", -3: "kernel launch failed", -4: "device configuration failed",
+          -5: "batch too large for the fixed scratch of pb_sample_noalloc"}
 
 ROW_OK, ROW_NONFINITE, ROW_BAD_UNIFORM, ROW_TIMEOUT, ROW_INTERNAL, ROW_BAD_PARAMS = 0, 1, 2, 4, 8, 16
 ROW_FALLBACK = 32
@@ -49,8 +50,20 @@ def record_bytes(cap: int) -> int:
     """Bytes of one row's candidate record (pb_record_bytes)."""
     return CAND_HEADER.itemsize + 8 * int(cap)
 
-EXPORTS = ("pb_sample", "pb_sample_ws", "pb_sample_ws_bytes", "pb_candidates", "pb_merge", "pb_record_bytes",
-           "pb_key_of", "pb_exp", "pb_strerror", "pb_version")
+EXPORTS = (
+    "pb_sample",
+    "pb_sample_ws",
+    "pb_sample_ws_bytes",
+    "pb_sample_noalloc",
+    "pb_sample_noalloc_max_bytes",
+    "pb_candidates",
+    "pb_merge",
+    "pb_record_bytes",
+    "pb_key_of",
+    "pb_exp",
+    "pb_strerror",
+    "pb_version",
+)
 
 _lib: ctypes.CDLL | None = None
 
@@ -79,6 +92,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     L.pb_sample.restype = i32
     L.pb_sample_ws.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp, i64, vp]
     L.pb_sample_ws.restype = i32
+    L.pb_sample_noalloc.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp]
+    L.pb_sample_noalloc.restype = i32
+    L.pb_sample_noalloc_max_bytes.argtypes = []
+    L.pb_sample_noalloc_max_bytes.restype = i64
     L.pb_sample_ws_bytes.argtypes = [i64, i64, i32]
     L.pb_sample_ws_bytes.restype = i64
     L.pb_candidates.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, i32, vp, vp]

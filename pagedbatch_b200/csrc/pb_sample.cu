@@ -2342,6 +2342,29 @@ int run_split(const void* logits, int dtype, int es, int64_t n_rows, int64_t voc
   if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
   return launch<__half>(a, C, st);
 }
+
+// ---- allocation-free entry point -------------------------------------------------------------
+// Some callers cannot allocate device memory at all: plugins whose host application owns every
+// byte of the GPU through its own allocator, or C callers with no allocator of their own. For
+// them pb_sample_noalloc runs the workspace path with this fixed array as its workspace. Every GPU
+// that loads this library holds the array until the process exits.
+constexpr int64_t NOALLOC_SCRATCH_BYTES = 32ll << 20;  // 32 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device (in host
+// code the array's name is only a host-side stand-in, never a device address).
+int noalloc_scratch(uint8_t** out) {
+  static uint8_t* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return PB_E_DEVICE;
+    addr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = addr[dev];
+  return PB_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -2452,6 +2475,29 @@ int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, i
                    static_cast<uint8_t*>(workspace), S, static_cast<cudaStream_t>(stream));
 }
 
+int64_t pb_sample_noalloc_max_bytes(void) { return NOALLOC_SCRATCH_BYTES; }
+
+int pb_sample_noalloc(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                      const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
+                      pb_row_info* out_info, void* stream) {
+  if (n_rows < 0 || vocab <= 0 || row_stride < vocab) return PB_E_INVALID;
+  if (vocab >= PB_MAX_VOCAB) return PB_E_TOO_LARGE;
+  if (n_rows == 0) return PB_OK;
+  if (!logits || !params || !out_token) return PB_E_INVALID;
+  if (n_rows > (int64_t)(0x7FFFFFFF / 8)) return PB_E_INVALID;
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  const int S = slices_for(n_rows, vocab, es);
+  if (ws_bytes_for(n_rows, S) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
+  uint8_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != PB_OK) return rc;
+  // every byte the launches read is written earlier in the same call: nothing needs clearing
+  return run_split(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info, scratch, S,
+                   static_cast<cudaStream_t>(stream));
+}
+
 uint32_t pb_key_of(float x) {
   if (x != x) return 0xFFFFFFFFu;
   uint32_t b;
@@ -2493,6 +2539,7 @@ const char* pb_strerror(int code) {
     case PB_E_TOO_LARGE: return "vocabulary too large (must be < 2^24)";
     case PB_E_LAUNCH: return "kernel launch failed";
     case PB_E_DEVICE: return "device configuration failed";
+    case PB_E_SCRATCH: return "batch needs more scratch than pb_sample_noalloc's fixed array holds";
     default: return "unknown error";
   }
 }
