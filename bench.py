@@ -353,9 +353,9 @@ def run_ours(args):
         "e2e": {"value": world * B / e2e_s, "unit": "rows/s", "ms_per_step": e2e_s * 1e3,
                 "h2d_bytes_per_step": alg_bytes + rec.nbytes, "d2h_bytes_per_step": 8 * B,
                 "api": "pagedbatch_b200.sample_tokens(pinned host logits)"},
-        # one launch per step; PB_PATH=split makes it three (slice scan, merge, full-row kernel on the
-        # rows the first two could not settle)
-        "gpu_launches": args.steps * (3 if ops._split_path() else 1),
+        # one launch per step; PB_PATH=pass makes it two (the persistent pass, then the full-row
+        # kernel on the rows the pass could not settle) after a memset of the pass's row counters
+        "gpu_launches": args.steps * (2 if ops._pass_path() else 1),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -108,6 +108,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 
 // Shared-memory fetch-add with acquire-release ordering at CTA scope; returns the old value.
+// plain arrival (no transaction bytes): completes the phase of a count-1 barrier by itself
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
   uint32_t old;
   asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(smem_addr(p)), "r"(v) : "memory");

@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -630,6 +631,36 @@ __device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq,
   __syncthreads();
 }
 
+// Lower bound of the k-th largest key the CTA holds when every thread offers one key it holds (0:
+// none): each warp sorts its 32 offers (bitonic, in registers), takes its ceil(k / NW)-th largest,
+// and the CTA takes the smallest of those, so the NW warps hold at least k keys at or above it.
+// k <= OFFER_KMAX. Every thread returns the same key. All threads call; the caller separates two
+// calls (and any other use of sh.red[3 * NW ...]) with a barrier.
+constexpr int OFFER_KMAX = 32 * NW;
+// k up to which thresholds come from the offer bound (above it the bound, the smallest of a few
+// offers per warp, is too loose to thin candidates out; an exact bisection takes those)
+constexpr int OFFER_PREFER = 16 * NW;
+__device__ uint32_t block_offer_bound(uint32_t key, int k, Shared& sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, key, stride);
+      const bool desc = (lane & size) == 0;
+      const bool lower = (lane & stride) == 0;
+      key = (lower == desc) ? max(key, o) : min(key, o);
+    }
+  }
+  const uint32_t kj = __shfl_sync(0xFFFFFFFFu, key, (k + NW - 1) / NW - 1);
+  if (lane == 0) sh.red[3 * NW + w] = kj;
+  __syncthreads();
+  uint32_t mn = 0xFFFFFFFFu;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) mn = min(mn, sh.red[3 * NW + i]);
+  return mn;
+}
+
 // ---- the kernel -------------------------------------------------------------------------
 
 // Raise the candidate threshold sh.thr_f to the tie floor of a lower bound of the kth_rank-th
@@ -638,6 +669,31 @@ __device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq,
 // separates two calls. Kept out of line so the streaming loop stays small.
 __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank, float tf, Shared& sh) {
   const int tid = threadIdx.x;
+  if (kth_rank <= OFFER_PREFER) {
+    // every thread offers its largest candidate; the bound only ever raises the threshold
+    uint32_t top = 0;
+#pragma unroll
+    for (int j = 0; j < SLOTS; ++j)
+      if (j < nc) top = max(top, comp_key(candB[j * NT + tid]));
+    const uint32_t lo = block_offer_bound(top, kth_rank, sh);
+    const float old = sh.thr_f;
+    __syncthreads();  // every thread has read the old threshold and sh.red
+    if (tid == 0 && lo > KEY_NEG_INF) sh.thr_f = fmaxf(old, tie_floor(value_of(lo), tf));
+    __syncthreads();
+    const uint32_t fk = key_of(sh.thr_f);
+    int w = 0;
+#pragma unroll
+    for (int j = 0; j < SLOTS; ++j) {
+      if (j < nc) {
+        const uint64_t c = candB[j * NT + tid];
+        if (comp_key(c) >= fk) {
+          candB[w * NT + tid] = c;
+          ++w;
+        }
+      }
+    }
+    return w;
+  }
   uint32_t kk[SLOTS];
   uint32_t mn = 0xFFFFFFFFu, mx = 0;
 #pragma unroll
@@ -693,6 +749,13 @@ __device__ __noinline__ void first_threshold(const uint4* buf, int nv, int top_k
   tmax = mx;  // this thread's maximum key (0 if it holds no value)
   const int holders = min(nv, NT);
   uint32_t k0;
+  if (top_k <= OFFER_PREFER) {
+    k0 = block_offer_bound(tmax, top_k, sh);
+    __syncthreads();  // sh.red read by every thread
+    if (tid == 0) sh.thr_f = (k0 > KEY_NEG_INF) ? tie_floor(value_of(k0), tf) : -INFINITY;
+    __syncthreads();
+    return;
+  }
   if (holders >= top_k) {
     uint32_t one[1] = {tmax};
     uint32_t unused, tmin, tmx;
@@ -1198,22 +1261,44 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           for (int i = tid; i < counts[r]; i += NT) candB[offs[r] + i] = L[i];
         }
       }
-      if (tid == 0) sh.nk = fits ? 0 : KCAP + 1;
+      if (tid == 0) {
+        sh.nk = fits ? 0 : KCAP + 1;
+        sh.bucket_kth = 0;
+      }
       __syncthreads();
       if (fits) {
-        uint32_t kk[SLOTS];
-        uint32_t mn = 0xFFFFFFFFu, mx = 0;
+        const uint32_t kq = (uint32_t)min(top_k, total);
+        uint32_t kth_raw;
+        if (total <= NT) {
+          // exact kq-th largest raw key by counting: the key with #greater < kq <= #greater-or-equal
+          // (every thread reads the same entry at a time: shared-memory broadcasts)
+          const uint32_t* hk = reinterpret_cast<const uint32_t*>(candB);  // high words: the keys
+          if (tid < total) {
+            const uint32_t mine = hk[2 * tid + 1];
+            uint32_t gt = 0, ge = 0;
+            for (int i = 0; i < total; ++i) {
+              const uint32_t b = hk[2 * i + 1];
+              gt += (b > mine) ? 1u : 0u;
+              ge += (b >= mine) ? 1u : 0u;
+            }
+            if (gt < kq && kq <= ge) atomicMax(&sh.bucket_kth, mine);  // the hits hold equal keys
+          }
+          __syncthreads();
+          kth_raw = sh.bucket_kth;
+        } else {
+          uint32_t kk[SLOTS];
+          uint32_t mn = 0xFFFFFFFFu, mx = 0;
 #pragma unroll
-        for (int j = 0; j < SLOTS; ++j) {
-          const int i = j * NT + tid;
-          kk[j] = (i < total) ? comp_key(candB[i]) : 0u;
-          if (i < total) mn = min(mn, kk[j]);
-          mx = max(mx, kk[j]);
+          for (int j = 0; j < SLOTS; ++j) {
+            const int i = j * NT + tid;
+            kk[j] = (i < total) ? comp_key(candB[i]) : 0u;
+            if (i < total) mn = min(mn, kk[j]);
+            mx = max(mx, kk[j]);
+          }
+          uint32_t unused, kmin, kmax;
+          block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+          kth_raw = block_kth_select<SLOTS>(kk, kq, kmin, (uint32_t)total, (uint64_t)kmax + 1, true, sh);
         }
-        uint32_t unused, kmin, kmax;
-        block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
-        const uint32_t kth_raw = block_kth_select<SLOTS>(kk, (uint32_t)min(top_k, total), kmin, (uint32_t)total,
-                                                         (uint64_t)kmax + 1, true, sh);
         const uint32_t kth = key_of(__fdiv_rn(value_of(kth_raw), tf));
         for (int i0 = 0; i0 < total; i0 += NT) {
           const int i = i0 + tid;
@@ -1868,318 +1953,508 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
   }
 }
 
-// ---- slice scan: the lean streaming stage of the three-launch path ----------------------------
+// ---- persistent pass: the workspace path --------------------------------------------------------
 //
-// pb_sample_ws runs a batch as scan_kernel (one CTA per row slice, no clusters, 48 KB of shared
-// memory and at most 64 registers, so 4 CTAs share an SM) -> merge_kernel (one CTA per row) ->
-// sample_kernel restricted to the rows the merge could not settle. The scan handles greedy rows and
-// top-k rows with k <= L_KMAX and writes the vocabulary-parallel record format: a slice is a shard.
+// pb_sample_ws runs a batch as pass_kernel -> sample_kernel restricted to the rows the pass could
+// not settle. pass_kernel is persistent (at most two CTAs per SM, no clusters). A row's body of
+// 16-byte vectors is cut into `parts` units of at most `cpu` staged chunks; CTA g takes units
+// g, g + grid, g + 2 grid, ... and streams them through one TMA ring that runs on across unit
+// boundaries, so the copies of the next unit are in flight while a unit is closed. A unit leaves a
+// candidate record in the vocabulary-parallel format (a unit is a shard of its row); the CTA that
+// closes a row's last unit merges the row's records at once, with the arithmetic of the full-row
+// small path, while the other CTAs keep streaming.
 
-constexpr int L_CHUNK_BYTES = 8192;                 // bytes per staged chunk
-constexpr int L_NSTAGE = 4;                         // ring depth
-constexpr int L_RING = L_CHUNK_BYTES * L_NSTAGE;    // 32 KB
-constexpr int L_SLOTS = 8;                          // candidate slots per thread
-constexpr int L_SMEM = L_RING + L_SLOTS * NT * 8;   // 48 KB
-constexpr int L_CAP = 1024;                         // entries per slice record
-constexpr int L_KMAX = 512;                         // largest top_k the scan resolves
-constexpr int L_CP_CHUNKS = 8;                      // chunks between CTA checkpoints
-static_assert(L_SLOTS <= SLOTS, "compact_slots walks at most SLOTS slots");
-static_assert(L_NSTAGE <= MAX_STAGE, "ring barriers live in Shared");
+constexpr int U_CAP = 512;      // entries per unit record
+constexpr int U_KMAX = 256;     // largest top_k the pass resolves (the first threshold needs k <= 32 * NW)
+constexpr int U_MAXPARTS = 64;  // units per row
+constexpr int U_MAXCPU = 8;     // staged chunks per unit
+constexpr int U_MERGE = 4096;   // union entries one merge holds (16 per thread)
+static_assert(SLOTS * NT >= KCAP, "a merge's survivors reuse the candidate slots");
+static_assert(U_MERGE % NT == 0, "the union splits evenly");
 
-struct ScanArgs {
+struct PassArgs {
   const char* logits;
   int64_t n_rows, vocab, row_stride;
   const int32_t* row_index;
   const pb_row_params* params;
-  int32_t slices;
-  uint8_t* records;  // [slices][n_rows][record_bytes(L_CAP)]
+  int32_t cpu;         // staged chunks per unit
+  int32_t parts;       // units per row
+  int64_t units;       // n_rows * parts
+  uint32_t* row_done;  // units closed per row; zero when the launch starts, zero again when it ends
+  uint8_t* records;    // [n_rows][parts][record_bytes(U_CAP)]
+  int64_t* out_token;
+  pb_row_info* out_info;  // every row: settled, or PB_ROW_FALLBACK for the full-row kernel
 };
 
+enum : int { U_SKIP = 0, U_BAD = 1, U_GREEDY = 2, U_FILTER = 3 };
+
+// What the pass does with a row: settle rejected parameters, stream greedy rows and top-k rows with
+// k <= U_KMAX, leave every other row to the full-row kernel.
+__device__ __forceinline__ int unit_mode(const pb_row_params& p, int64_t V) {
+  const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
+  if (bad) return U_BAD;
+  if (p.temperature == 0.0) return U_GREEDY;
+  if (p.top_k > 0 && (int64_t)p.top_k < V && p.top_k <= U_KMAX) return U_FILTER;
+  return U_SKIP;
+}
+
+// Unit u of the batch: row item = u / parts, part = u % parts. Its vectors are [v0, v0 + nv) of the
+// row's 16-byte-aligned body (element vec_e0 onwards); part 0 also owns the scalar head, the last
+// part the scalar tail.
 template <typename T>
-__global__ void __launch_bounds__(NT, 4) scan_kernel(ScanArgs a) {
+struct UnitGeom {
+  int64_t item;
+  const T* row;
+  int64_t head_n, vec_e0, tail_e0, tail_n, e_first;
+  int32_t nv;
+  __device__ UnitGeom(const PassArgs& a, int64_t u) {
+    constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
+    item = u / a.parts;
+    const int part = (int)(u - item * a.parts);
+    const int64_t V = a.vocab;
+    const int64_t row_id = a.row_index ? (int64_t)a.row_index[item] : item;
+    row = reinterpret_cast<const T*>(a.logits) + row_id * a.row_stride;
+    int64_t head = (int64_t)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / ES);
+    if (head > V) head = V;
+    const int64_t nvec_all = (V - head) / EPV;
+    const int64_t uv = (int64_t)a.cpu * (CHUNK_BYTES / 16);
+    const int64_t v0 = min(nvec_all, (int64_t)part * uv);
+    nv = (int32_t)(min(nvec_all, v0 + uv) - v0);
+    vec_e0 = head + v0 * EPV;
+    head_n = (part == 0) ? head : 0;
+    tail_e0 = head + nvec_all * EPV;
+    tail_n = (part == a.parts - 1) ? V - tail_e0 : 0;
+    e_first = (part == 0) ? 0 : vec_e0;
+  }
+};
+
+// Lower bound of a unit's top_k-th value from its first staged chunk: each warp's
+// ceil(top_k / NW)-th largest per-thread maximum, smallest over the warps (the NW warps then hold
+// at least top_k values at or above it; padding counts as -inf, which only lowers the bound).
+// Returns its tie floor. All threads call.
+template <int VPT>
+__device__ float unit_threshold(const float (&vm)[VPT], int top_k, float tf, Shared& sh) {
+  float mx = vm[0];
+#pragma unroll
+  for (int j = 1; j < VPT; ++j) mx = fmax_nan(mx, vm[j]);
+  const uint32_t lo = block_offer_bound(key_of(mx), top_k, sh);
+  __syncthreads();  // sh.red read by every thread
+  if (threadIdx.x == 0) sh.thr_f = (lo > KEY_NEG_INF) ? tie_floor(value_of(lo), tf) : -INFINITY;
+  __syncthreads();
+  return sh.thr_f;
+}
+
+// Merge one row from its units' records (the row's last unit was just closed by this CTA), with the
+// steps of merge_kernel: union of the survivors, exact top_k-th key, then finish_survivors. The
+// records are read through L2 only (other CTAs wrote them during this launch). K (KCAP entries)
+// holds the survivors. All threads call.
+__device__ void pass_merge(const PassArgs& a, int64_t item, const pb_row_params& p, uint64_t* K, Shared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int P = a.parts;
+  const int64_t rb = record_bytes(U_CAP);
+  const uint8_t* base = a.records + item * P * rb;
+  __shared__ uint32_t uoff[U_MAXPARTS + 1];
+  __shared__ int32_t w_fl[NW];
+  __shared__ float w_hm[NW], w_gk[NW];
+  __shared__ uint64_t w_gb[NW];
+
+  int32_t fl = 0, cnt = 0;
+  float hm = -INFINITY, gk = -INFINITY;
+  uint64_t gb = 0;
+  if (tid < P) {
+    const int4 h = __ldcg(reinterpret_cast<const int4*>(base + tid * rb));
+    cnt = h.x;
+    fl = h.y;
+    hm = __int_as_float(h.z);
+    if ((fl & PB_CAND_GREEDY) && cnt == 1) {
+      gb = __ldcg(reinterpret_cast<const unsigned long long*>(base + tid * rb + sizeof(pb_cand_header)));
+      gk = hm;
+    }
+  }
+  uint32_t total;
+  const uint32_t off = block_excl_scan<uint32_t, NT>((uint32_t)cnt, sh.s32, &total);
+  if (tid < P) uoff[tid] = off;
+  if (tid == 0) uoff[P] = total;
+  fl = (int32_t)__reduce_or_sync(0xFFFFFFFFu, (uint32_t)fl);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    hm = fmax_nan(hm, __shfl_xor_sync(0xFFFFFFFFu, hm, o));
+    const uint64_t gb2 = __shfl_xor_sync(0xFFFFFFFFu, gb, o);
+    const float gk2 = __shfl_xor_sync(0xFFFFFFFFu, gk, o);
+    if (gb2 > gb) {
+      gb = gb2;
+      gk = gk2;
+    }
+  }
+  if (lane == 0) {
+    w_fl[w] = fl;
+    w_hm[w] = hm;
+    w_gb[w] = gb;
+    w_gk[w] = gk;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int i = 1; i < NW; ++i) {
+      fl |= w_fl[i];
+      hm = fmax_nan(hm, w_hm[i]);
+      if (w_gb[i] > gb) {
+        gb = w_gb[i];
+        gk = w_gk[i];
+      }
+    }
+    const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
+    const uint32_t mk = key_of(hm);
+    int mode = 0;  // 0 status only, 1 greedy, 2 merge
+    sh.status = PB_ROW_OK;
+    if (fl & PB_ROW_TIMEOUT) sh.status = PB_ROW_TIMEOUT;
+    else if (bad) sh.status = PB_ROW_BAD_PARAMS;
+    else if (p.temperature == 0.0) mode = 1;
+    else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) sh.status = PB_ROW_NONFINITE;
+    else if (!(p.uniform >= 0.0 && p.uniform < 1.0)) sh.status = PB_ROW_BAD_UNIFORM;
+    else if ((fl & (PB_CAND_FALLBACK | 0xFF)) || total > (uint32_t)U_MERGE || total == 0) sh.status = PB_ROW_FALLBACK;
+    else mode = 2;
+    if (mode == 1 && (fl & ~PB_CAND_GREEDY)) {  // a unit could not publish its maximum (a NaN)
+      sh.status = PB_ROW_FALLBACK;
+      mode = 0;
+    }
+    sh.nk = mode;
+    sh.row_max = hm;
+    sh.row_best = gk;
+    sh.arg = comp_idx(gb);
+  }
+  __syncthreads();
+  const int mode = sh.nk;
+  pb_row_info info = {};
+  int64_t token = -1;
+  info.status = sh.status;
+  if (mode == 1) {
+    info.max_key = sh.row_best;
+    info.thr_key = key_of(info.max_key);
+    info.n_tie_kept = 1;
+    info.kept_count = 1;
+    info.flags = PB_PATH_GREEDY;
+    token = sh.arg;
+  } else if (mode == 2) {
+    const float m = sh.row_max;
+    info.max_key = m;
+    auto entry = [&](uint32_t i) {  // union entry i (i < total): its unit is the last with uoff <= i
+      int lo = 0, hi = P;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (uoff[mid] <= i) lo = mid;
+        else hi = mid;
+      }
+      return __ldcg(reinterpret_cast<const unsigned long long*>(base + lo * rb + sizeof(pb_cand_header)) +
+                    (i - uoff[lo]));
+    };
+    constexpr int NJ = U_MERGE / NT;
+    uint32_t kk[NJ];
+    uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const uint32_t i = (uint32_t)(j * NT + tid);
+      kk[j] = (i < total) ? comp_key(entry(i)) : 0u;
+      if (i < total) mn = min(mn, kk[j]);
+      mx = max(mx, kk[j]);
+    }
+    uint32_t unused, kmin, kmax;
+    block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
+    const uint32_t kq = (uint32_t)min((int64_t)p.top_k, (int64_t)total);
+    const uint32_t kth = block_kth_select<NJ>(kk, kq, kmin, total, (uint64_t)kmax + 1, true, sh);
+    if (tid == 0) sh.nk = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const uint32_t i = (uint32_t)(j * NT + tid);
+      const bool pass = i < total && kk[j] >= kth;
+      const uint32_t idx = pass ? comp_idx(entry(i)) : 0u;
+      warp_append(pass, kk[j], idx, K, &sh.nk, KCAP);
+    }
+    __syncthreads();
+    const int nk = sh.nk;
+    if (nk <= KCAP) {
+      const bool topp_active = p.top_p < 1.0 && (float)p.top_p < 1.0f;
+      finish_survivors(K, nk, m, topp_active, (float)p.top_p, (uint64_t)(p.uniform * 0x1p53), sh, &token, &info);
+    } else if (tid == 0) {
+      info.status = PB_ROW_FALLBACK;
+    }
+  } else if (sh.status == PB_ROW_NONFINITE || sh.status == PB_ROW_BAD_UNIFORM || sh.status == PB_ROW_TIMEOUT) {
+    info.max_key = sh.row_max;
+  }
+  if (tid == 0) {
+    a.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
+    pb_row_info* o = a.out_info + item;
+    o->thr_key = info.thr_key;
+    o->n_tie_kept = info.n_tie_kept;
+    o->kept_count = info.kept_count;
+    o->status = info.status;
+    o->max_key = info.max_key;
+    o->flags = info.flags;
+    o->z_q = info.z_q;
+    o->kept_q = info.kept_q;
+  }
+  __syncthreads();  // K and the shared scratch are free again
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT, 2) pass_kernel(PassArgs a) {
   constexpr int EPV = Elem<T>::EPV;
-  constexpr int CV = L_CHUNK_BYTES / 16;  // vectors per chunk
-  constexpr int VPT = CV / NT;            // vectors per thread per chunk
-  static_assert(CV % NT == 0, "chunk must split evenly");
+  constexpr int CV = CHUNK_BYTES / 16;  // vectors per chunk
+  constexpr int VPT = CV / NT;          // vectors per thread per chunk
+  constexpr int NSTAGE = RING_BYTES / CHUNK_BYTES;
   extern __shared__ __align__(128) unsigned char dyn[];
   __shared__ Shared sh;
+  __shared__ int32_t s_last;
+  __shared__ float lwf[NW], lwm[NW];
+  __shared__ uint32_t lwi[NW];
   uint4* ring = reinterpret_cast<uint4*>(dyn);
-  uint64_t* slots = reinterpret_cast<uint64_t*>(dyn + L_RING);
-  const int S = a.slices;
-  const int64_t item = blockIdx.x / S;
-  const int rank = (int)(blockIdx.x % S);
+  uint64_t* slots = reinterpret_cast<uint64_t*>(dyn + RING_BYTES);
   const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t G = gridDim.x;
   const int64_t V = a.vocab;
-  uint8_t* rec = a.records + ((int64_t)rank * a.n_rows + item) * record_bytes(L_CAP);
-  pb_cand_header* hdr = reinterpret_cast<pb_cand_header*>(rec);
-  uint64_t* ent = reinterpret_cast<uint64_t*>(rec + sizeof(pb_cand_header));
+  const int cpu = a.cpu;
+  const int64_t my_units = (a.units - (int64_t)blockIdx.x + G - 1) / G;
+  const int64_t nseq = my_units * cpu;  // chunks this CTA walks (empty ones complete at once)
 
-  const pb_row_params p = a.params[item];
-  const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
-  const bool greedy = !bad && p.temperature == 0.0;
-  const bool filtering = !bad && !greedy && p.top_k > 0 && (int64_t)p.top_k < V && p.top_k <= L_KMAX;
-  if (!greedy && !filtering) {
-    // rejected parameters are settled by the merge; every other row needs the full-row sampler
-    if (tid == 0) {
-      hdr->count = 0;
-      hdr->flags = bad ? PB_ROW_BAD_PARAMS : PB_CAND_FALLBACK;
-      hdr->max_key = 0.0f;
-      hdr->reserved = 0;
-    }
-    return;
-  }
-  const float tf = (float)p.temperature;
-  const int32_t top_k = p.top_k;
-  const int64_t row_id = a.row_index ? (int64_t)a.row_index[item] : item;
-  const T* row = reinterpret_cast<const T*>(a.logits) + row_id * a.row_stride;
-  const Slice s = make_slice(row, V, rank, S);
   if (tid == 0) {
-    for (int st = 0; st < L_NSTAGE; ++st) {
+    for (int st = 0; st < NSTAGE; ++st) {
       mbar_init(&sh.mbar[st], 1);
       sh.stage_chunk[st] = -1;
       sh.released[st] = 0;
     }
-    sh.cp_flags[0] = sh.cp_flags[1] = sh.cp_flags[2] = 0;
-    sh.cp_count[0] = sh.cp_count[1] = sh.cp_count[2] = 0;
-    sh.thr_f = -INFINITY;
     fence_mbar_init();
   }
   __syncthreads();
 
-  float runmax = -INFINITY, bestv = -INFINITY;
-  uint32_t bidx = 0xFFFFFFFFu;
-  int nc = 0;
-  bool ovf = false, row_ovf = false;
-  auto push = [&](float x, uint32_t e) {
-    if (nc < L_SLOTS) {
-      slots[nc * NT + tid] = compose(key_of(x), e);
-      ++nc;
+  // stage chunk `seq` of this CTA's walk: a bulk copy, or an empty arrival when the unit has no
+  // such chunk or its row is not streamed
+  auto issue = [&](int64_t seq) {
+    const int st = (int)(seq % NSTAGE);
+    const int64_t i = seq / cpu;
+    const int cc = (int)(seq - i * cpu);
+    const UnitGeom<T> g(a, (int64_t)blockIdx.x + i * G);
+    const int mode = unit_mode(a.params[g.item], V);
+    const int n = (mode == U_GREEDY || mode == U_FILTER) ? max(0, min(CV, g.nv - cc * CV)) : 0;
+    sh.stage_chunk[st] = seq;
+    if (n > 0) {
+      mbar_expect_tx(&sh.mbar[st], (uint32_t)(n * 16));
+      bulk_load(ring + st * CV, reinterpret_cast<const uint4*>(g.row + g.vec_e0) + (int64_t)cc * CV, (uint32_t)(n * 16),
+                &sh.mbar[st], l2_policy_evict_first());
     } else {
-      ovf = true;
+      mbar_arrive(&sh.mbar[st]);
     }
-  };
-  for (int64_t e = tid; e < s.head_n; e += NT) {
-    const float x = Elem<T>::ld(row + e);
-    runmax = fmax_nan(runmax, x);
-    if (greedy && x > bestv) {
-      bestv = x;
-      bidx = (uint32_t)e;
-    }
-  }
-  const int nch = (int)((s.nvec + CV - 1) / CV), nvec32 = (int)s.nvec;
-  const uint4* src = reinterpret_cast<const uint4*>(row + s.vec_e0);
-  auto issue = [&](int c) {
-    const int st = c % L_NSTAGE;
-    const int nv = min(CV, nvec32 - c * CV);
-    sh.stage_chunk[st] = c;
-    mbar_expect_tx(&sh.mbar[st], (uint32_t)(nv * 16));
-    bulk_load(ring + st * CV, src + (int64_t)c * CV, (uint32_t)(nv * 16), &sh.mbar[st], l2_policy_evict_first());
   };
   if (tid == 0)
-    for (int c = 0; c < L_NSTAGE && c < nch; ++c) issue(c);
-  bool timed_out = false, cta_timeout = false;
-  if (filtering && nch > 0) {
-    // first threshold from the first chunk (it stays staged for the loop below)
-    timed_out = !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sh.mbar[0], 0u, WAIT_POLLS));
-    const int nv0 = min(CV, nvec32);
-    if (nv0 * EPV >= top_k) first_threshold<T, VPT>(ring, nv0, top_k, tf, sh);
-  }
-  float t = sh.thr_f;
-  const uint32_t e_base = (uint32_t)s.vec_e0 + (uint32_t)tid * EPV;
-  int cp = 0;
-  for (int c = 0; c < nch; ++c) {
-    const int stage = c % L_NSTAGE;
-    if (!timed_out)
-      timed_out = !__all_sync(0xFFFFFFFFu,
-                              mbar_wait_bounded(&sh.mbar[stage], (uint32_t)((c / L_NSTAGE) & 1), WAIT_POLLS));
-    const int nv = min(CV, nvec32 - c * CV);
-    const uint4* buf = ring + stage * CV;
-    float x[VPT][EPV];
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int v = j * NT + tid;
-      if (v < nv && !timed_out) {
-        Elem<T>::unpack(buf[v], x[j]);
+    for (int64_t s = 0; s < NSTAGE && s < nseq; ++s) issue(s);
+
+  bool timed_out = false;    // this warp gave up waiting (warp-uniform)
+  bool cta_timeout = false;  // some warp of the CTA gave up (CTA-uniform)
+  for (int64_t i = 0; i < my_units; ++i) {
+    const int64_t u = (int64_t)blockIdx.x + i * G;
+    const UnitGeom<T> g(a, u);
+    const pb_row_params p = a.params[g.item];
+    const int mode = unit_mode(p, V);
+    const bool greedy = mode == U_GREEDY, filtering = mode == U_FILTER;
+    const float tf = (float)p.temperature;
+    const int32_t top_k = p.top_k;
+    float runmax = -INFINITY, bestv = -INFINITY;
+    uint32_t bidx = 0xFFFFFFFFu;
+    int nc = 0;
+    bool ovf = false;
+    float t = -INFINITY;  // candidate threshold of this unit
+    auto push = [&](float x, uint32_t e) {
+      if (nc < SLOTS) {
+        slots[nc * NT + tid] = compose(key_of(x), e);
+        ++nc;
       } else {
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) x[j][q] = -INFINITY;
+        ovf = true;
       }
-    }
-    __syncwarp();
-    if (lane == 0 && !timed_out) {
-      // this warp is done with the stage; the last warp to release it refills it
-      if (atom_add_acq_rel(&sh.released[stage], 1u) == NW - 1) {
-        sh.released[stage] = 0;
-        if (c + L_NSTAGE < nch) {
-          fence_proxy_async();
-          issue(c + L_NSTAGE);
-        }
-      }
-    }
-    float vm[VPT];
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      float m2 = fmax_nan(x[j][0], x[j][1]);
-#pragma unroll
-      for (int q = 2; q < EPV; ++q) m2 = fmax_nan(m2, x[j][q]);
-      vm[j] = m2;
-      runmax = fmax_nan(runmax, m2);
-    }
-    if (greedy) {
+    };
+    const uint32_t e_base = (uint32_t)g.vec_e0 + (uint32_t)tid * EPV;
+    for (int cc = 0; cc < cpu; ++cc) {
+      const int64_t seq = i * cpu + cc;
+      const int stage = (int)(seq % NSTAGE);
+      const uint32_t parity = (uint32_t)((seq / NSTAGE) & 1);
+      if (!timed_out) timed_out = !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sh.mbar[stage], parity, WAIT_POLLS));
+      const int n = (greedy || filtering) ? max(0, min(CV, g.nv - cc * CV)) : 0;
+      const uint4* buf = ring + stage * CV;
+      float x[VPT][EPV];
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        if (vm[j] > bestv) {
-          bestv = vm[j];
-          int jj = EPV - 1;
+        if (j * NT + tid < n && !timed_out) {
+          Elem<T>::unpack(buf[j * NT + tid], x[j]);
+        } else {
 #pragma unroll
-          for (int q = EPV - 1; q >= 0; --q)
-            if (x[j][q] == vm[j]) jj = q;
-          bidx = e_base + (uint32_t)((c * CV + j * NT) * EPV + jj);
+          for (int q = 0; q < EPV; ++q) x[j][q] = -INFINITY;
         }
       }
-    } else if (!row_ovf) {
+      __syncwarp();
+      if (lane == 0 && !timed_out) {
+        // this warp is done with the stage; the last warp to release it refills it
+        if (atom_add_acq_rel(&sh.released[stage], 1u) == NW - 1) {
+          sh.released[stage] = 0;
+          if (seq + NSTAGE < nseq) {
+            fence_proxy_async();
+            issue(seq + NSTAGE);
+          }
+        }
+      }
+      if (n == 0) continue;  // the same for every thread
+      float vm[VPT];
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        if (j * NT + tid < nv && vm[j] >= t) {  // vectors past the chunk's end hold -inf padding
-          const uint32_t e0 = e_base + (uint32_t)((c * CV + j * NT) * EPV);
+        float m2 = fmax_nan(x[j][0], x[j][1]);
 #pragma unroll
-          for (int q = 0; q < EPV; ++q)
-            if (x[j][q] >= t) push(x[j][q], e0 + q);
+        for (int q = 2; q < EPV; ++q) m2 = fmax_nan(m2, x[j][q]);
+        vm[j] = m2;
+        runmax = fmax_nan(runmax, m2);
+      }
+      if (greedy) {
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          if (vm[j] > bestv) {
+            bestv = vm[j];
+            int jj = EPV - 1;
+#pragma unroll
+            for (int q = EPV - 1; q >= 0; --q)
+              if (x[j][q] == vm[j]) jj = q;
+            bidx = e_base + (uint32_t)((cc * CV + j * NT) * EPV + jj);
+          }
+        }
+      } else if (filtering) {
+        if (cc == 0) t = unit_threshold<VPT>(vm, top_k, tf, sh);
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          if (j * NT + tid < n && vm[j] >= t) {
+            const uint32_t e0 = e_base + (uint32_t)((cc * CV + j * NT) * EPV);
+#pragma unroll
+            for (int q = 0; q < EPV; ++q)
+              if (x[j][q] >= t) push(x[j][q], e0 + q);
+          }
         }
       }
     }
-    if (c % L_CP_CHUNKS == L_CP_CHUNKS - 1 || c == nch - 1) {
-      // checkpoint; flag and count words rotate over three slots so a reset never races a write
-      const int mine = (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && nc >= L_SLOTS / 2) ? 1 : 0);
-      if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
-      if (filtering) {
-        const uint32_t wsum = __reduce_add_sync(0xFFFFFFFFu, (uint32_t)nc);
-        if (lane == 0 && wsum) atomicAdd(&sh.cp_count[cp % 3], wsum);
-      }
-      __syncthreads();
-      const int f = sh.cp_flags[cp % 3];
-      const uint32_t held = sh.cp_count[cp % 3];
-      if (tid == 0) {
-        sh.cp_flags[(cp + 2) % 3] = 0;
-        sh.cp_count[(cp + 2) % 3] = 0;
-      }
-      ++cp;
-      if (f & 4) {
-        cta_timeout = true;
-        break;
-      }
-      if (f & 2) row_ovf = true;
-      if (((f & 1) || held >= (uint32_t)(4 * top_k + 64)) && !row_ovf) nc = compact_slots(slots, nc, top_k, tf, sh);
-      t = sh.thr_f;  // every thread passed the barrier after any write of the threshold
+    // scalar head (part 0) and tail (last part)
+    if ((greedy || filtering) && !cta_timeout) {
+      auto visit = [&](int64_t e) {
+        const float x = Elem<T>::ld(g.row + e);
+        runmax = fmax_nan(runmax, x);
+        if (greedy && x > bestv) {
+          bestv = x;
+          bidx = (uint32_t)e;
+        }
+        if (filtering && x >= t) push(x, (uint32_t)e);
+      };
+      for (int64_t e = tid; e < g.head_n; e += NT) visit(e);
+      for (int64_t e = tid; e < g.tail_n; e += NT) visit(g.tail_e0 + e);
     }
-  }
-  if (cta_timeout) {
-    // let every issued copy land before the block leaves
-    if (tid == 0)
-      for (int st = 0; st < L_NSTAGE; ++st) {
-        const int64_t c = sh.stage_chunk[st];
-        if (c >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((c / L_NSTAGE) & 1), WAIT_POLLS);
+    if (__syncthreads_or(timed_out)) cta_timeout = true;
+    timed_out = cta_timeout;  // after a timeout no warp waits again
+    const bool unit_ovf = __syncthreads_or(ovf) != 0;
+    // CTA reduction: NaN-propagating max, first maximum
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bestv, o);
+      const uint32_t i2 = __shfl_xor_sync(0xFFFFFFFFu, bidx, o);
+      if (v2 > bestv || (v2 == bestv && i2 < bidx)) {
+        bestv = v2;
+        bidx = i2;
       }
+      runmax = fmax_nan(runmax, __shfl_xor_sync(0xFFFFFFFFu, runmax, o));
+    }
+    if (lane == 0) {
+      lwf[tid >> 5] = bestv;
+      lwi[tid >> 5] = bidx;
+      lwm[tid >> 5] = runmax;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if (lwf[w] > bestv || (lwf[w] == bestv && lwi[w] < bidx)) {
+        bestv = lwf[w];
+        bidx = lwi[w];
+      }
+      runmax = fmax_nan(runmax, lwm[w]);
+    }
+    __syncthreads();  // lwf/lwi/lwm are read before the next unit writes them
+
+    // this unit's record
+    uint8_t* rec = a.records + u * record_bytes(U_CAP);
+    pb_cand_header* hdr = reinterpret_cast<pb_cand_header*>(rec);
+    uint64_t* ent = reinterpret_cast<uint64_t*>(rec + sizeof(pb_cand_header));
+    int32_t h_count = 0, h_flags = 0;
+    float h_max = 0.0f;
+    if (cta_timeout) {
+      h_flags = PB_ROW_TIMEOUT;
+    } else if (mode == U_BAD) {
+      h_flags = PB_ROW_BAD_PARAMS;
+    } else if (mode == U_SKIP) {
+      h_flags = PB_CAND_FALLBACK;
+    } else if (greedy) {
+      h_max = bestv;
+      if (runmax != runmax) {
+        h_flags = PB_CAND_FALLBACK;  // a NaN: the full-row kernel finds the first one
+      } else {
+        h_flags = PB_CAND_GREEDY;
+        if (g.nv > 0 || g.head_n > 0 || g.tail_n > 0) {
+          // every value -inf: the unit's first index stands for its maximum
+          if (tid == 0) ent[0] = compose(key_of(bestv), (bidx == 0xFFFFFFFFu) ? (uint32_t)g.e_first : bidx);
+          h_count = 1;
+        }
+      }
+    } else {
+      const float m = __fdiv_rn(runmax, tf);
+      h_max = m;
+      if (key_of(m) >= KEY_POS_INF) {
+        h_flags = PB_ROW_NONFINITE;  // NaN or +inf: so is the whole row
+      } else if (unit_ovf) {
+        h_flags = PB_CAND_FALLBACK;
+      } else {
+        uint32_t tot;
+        uint32_t pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
+        if (tot > (uint32_t)U_CAP) {  // crowded: shrink to about this unit's top_k first
+          nc = compact_slots(slots, nc, top_k, tf, sh);
+          pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
+        }
+        if (tot <= (uint32_t)U_CAP) {
+          for (int j = 0; j < nc; ++j) {
+            const uint64_t cv = slots[j * NT + tid];
+            ent[pos + j] = compose(key_of(__fdiv_rn(value_of(comp_key(cv)), tf)), comp_idx(cv));
+          }
+          h_count = (int32_t)tot;
+        } else {
+          h_flags = PB_CAND_FALLBACK;
+        }
+      }
+    }
+    if (tid == 0) {
+      hdr->count = h_count;
+      hdr->flags = h_flags;
+      hdr->max_key = h_max;
+      hdr->reserved = 0;
+    }
+    // close the unit: the CTA that closes a row's last unit merges the row (the barrier orders the
+    // CTA's record writes before thread 0's device-scope fence and arrival)
     __syncthreads();
     if (tid == 0) {
-      hdr->count = 0;
-      hdr->flags = PB_ROW_TIMEOUT;
-      hdr->max_key = 0.0f;
-      hdr->reserved = 0;
-    }
-    return;
-  }
-  for (int64_t e = tid; e < s.tail_n; e += NT) {
-    const float x = Elem<T>::ld(row + s.tail_e0 + e);
-    runmax = fmax_nan(runmax, x);
-    if (greedy && x > bestv) {
-      bestv = x;
-      bidx = (uint32_t)(s.tail_e0 + e);
-    }
-  }
-  if (filtering) {
-    // head and tail elements against the final threshold
-    for (int64_t e = tid; e < s.head_n; e += NT) {
-      const float x = Elem<T>::ld(row + e);
-      if (x >= t) push(x, (uint32_t)e);
-    }
-    for (int64_t e = tid; e < s.tail_n; e += NT) {
-      const float x = Elem<T>::ld(row + s.tail_e0 + e);
-      if (x >= t) push(x, (uint32_t)(s.tail_e0 + e));
-    }
-    if (__syncthreads_or(ovf)) row_ovf = true;
-  }
-  // CTA reduction: NaN-propagating max, first maximum (greedy)
-  for (int o = 16; o > 0; o >>= 1) {
-    const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bestv, o);
-    const uint32_t i2 = __shfl_xor_sync(0xFFFFFFFFu, bidx, o);
-    if (v2 > bestv || (v2 == bestv && i2 < bidx)) {
-      bestv = v2;
-      bidx = i2;
-    }
-    runmax = fmax_nan(runmax, __shfl_xor_sync(0xFFFFFFFFu, runmax, o));
-  }
-  __shared__ float lwf[NW], lwm[NW];
-  __shared__ uint32_t lwi[NW];
-  if (lane == 0) {
-    lwf[tid >> 5] = bestv;
-    lwi[tid >> 5] = bidx;
-    lwm[tid >> 5] = runmax;
-  }
-  __syncthreads();
-  for (int w = 0; w < NW; ++w) {
-    if (lwf[w] > bestv || (lwf[w] == bestv && lwi[w] < bidx)) {
-      bestv = lwf[w];
-      bidx = lwi[w];
-    }
-    runmax = fmax_nan(runmax, lwm[w]);
-  }
-  if (greedy) {
-    if (tid == 0) {
-      int32_t count = 0, flags = PB_CAND_GREEDY;
-      if (runmax != runmax) {
-        flags = PB_CAND_FALLBACK;  // a NaN: the full-row sampler finds the first one
-      } else if (s.e_hi > s.e_lo) {
-        // every value -inf: the slice's first index stands for its maximum
-        ent[0] = compose(key_of(bestv), (bidx == 0xFFFFFFFFu) ? (uint32_t)s.e_lo : bidx);
-        count = 1;
+      __threadfence();
+      const uint32_t done = atomicAdd(&a.row_done[g.item], 1u) + 1u;
+      const bool last = done == (uint32_t)a.parts;
+      if (last) {
+        a.row_done[g.item] = 0u;  // no other unit of this row is left in this launch
+        __threadfence();
       }
-      hdr->count = count;
-      hdr->flags = flags;
-      hdr->max_key = bestv;
-      hdr->reserved = 0;
+      s_last = last ? 1 : 0;
     }
-    return;
+    __syncthreads();
+    if (s_last) pass_merge(a, g.item, p, slots, sh);
   }
-  const float m = __fdiv_rn(runmax, tf);
-  const uint32_t mk = key_of(m);
-  int32_t flags = 0;
-  if (mk >= KEY_POS_INF) flags = PB_ROW_NONFINITE;                  // NaN or +inf: so is the whole row
-  else if (mk <= KEY_NEG_INF || row_ovf) flags = PB_CAND_FALLBACK;  // all -inf here, or too many ties
-  if (flags) {
-    if (tid == 0) {
-      hdr->count = 0;
-      hdr->flags = flags;
-      hdr->max_key = m;
-      hdr->reserved = 0;
+  if (cta_timeout && tid == 0) {
+    // let every issued copy land before the CTA leaves
+    for (int st = 0; st < NSTAGE; ++st) {
+      const int64_t c = sh.stage_chunk[st];
+      if (c >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((c / NSTAGE) & 1), WAIT_POLLS);
     }
-    return;
-  }
-  // shrink to (about) this slice's top_k, then publish with scaled keys and global indices
-  nc = compact_slots(slots, nc, top_k, tf, sh);
-  uint32_t tot;
-  const uint32_t pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
-  if (tot <= (uint32_t)L_CAP) {
-    for (int j = 0; j < nc; ++j) {
-      const uint64_t cv = slots[j * NT + tid];
-      ent[pos + j] = compose(key_of(__fdiv_rn(value_of(comp_key(cv)), tf)), comp_idx(cv));
-    }
-  }
-  if (tid == 0) {
-    hdr->count = (tot <= (uint32_t)L_CAP) ? (int32_t)tot : 0;
-    hdr->flags = (tot <= (uint32_t)L_CAP) ? 0 : PB_CAND_FALLBACK;
-    hdr->max_key = m;
-    hdr->reserved = 0;
   }
 }
 
@@ -2258,28 +2533,7 @@ int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32
   return PB_OK;
 }
 
-template <typename T>
-int launch_scan(const ScanArgs& a, cudaStream_t stream) {
-  static unsigned long long configured = 0;  // bit d: device d configured
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
-  if (!(configured & (1ull << dev))) {
-    if (cudaFuncSetAttribute(scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, L_SMEM) != cudaSuccess)
-      return PB_E_DEVICE;
-    configured |= 1ull << dev;
-  }
-  scan_kernel<T><<<(unsigned)(a.n_rows * a.slices), NT, L_SMEM, stream>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
-  return PB_OK;
-}
-
-// Slices per row for the scan: about four CTAs per SM over the batch, slices of at least 32 KB.
-int slices_for(int64_t n_rows, int64_t vocab, int es) {
-  const char* env = getenv("PB_SLICES");
-  if (env) {
-    const int c = atoi(env);
-    if (c == 1 || c == 2 || c == 4 || c == 8) return c;
-  }
+int sm_count() {
   static int sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -2289,39 +2543,123 @@ int slices_for(int64_t n_rows, int64_t vocab, int es) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     sms[dev] = n;
   }
-  const int64_t want = 4 * (int64_t)sms[dev];
-  const int64_t bytes = vocab * es;
-  int S = 1;
-  while (S < 8 && n_rows * 2 * S <= want && bytes / (2 * S) >= 32768) S <<= 1;
-  return S;
+  return sms[dev];
 }
 
-// workspace of pb_sample_ws: the slices' records, then the merge's per-row info
-int64_t ws_bytes_for(int64_t n_rows, int S) {
-  return (int64_t)S * n_rows * record_bytes(L_CAP) + n_rows * (int64_t)sizeof(pb_row_info);
+constexpr int PASS_SMEM = RING_BYTES + SLOTS * NT * 8;
+
+// Resident pass CTAs per SM (the grid is one wave of them); 1 when the query fails.
+int pass_ctas_per_sm(int es) {
+  static int occ[64][2] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  const int which = (es == 4) ? 0 : 1;
+  if (!occ[dev][which]) {
+    int n = 0;
+    cudaError_t rc;
+    if (es == 4) {
+      cudaFuncSetAttribute(pass_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
+      rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pass_kernel<float>, NT, PASS_SMEM);
+    } else {
+      cudaFuncSetAttribute(pass_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
+      cudaFuncSetAttribute(pass_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
+      rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pass_kernel<__nv_bfloat16>, NT, PASS_SMEM);
+    }
+    occ[dev][which] = (rc == cudaSuccess && n > 0) ? n : 1;
+  }
+  return occ[dev][which];
 }
 
-// scan -> merge -> full-row kernel on the rows the merge left as PB_ROW_FALLBACK (see pb_sample_ws)
-int run_split(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
-              const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
-              uint8_t* workspace, int S, cudaStream_t st) {
-  uint8_t* records = workspace;
+// Geometry of a pass launch: staged chunks per unit, units per row, total units, grid.
+struct PassPlan {
+  int cpu = 0, parts = 0;
+  int64_t units = 0, grid = 0;
+};
+
+// The unit size that minimises the busiest CTA's walk: rounds of units times (chunks per unit plus
+// half a chunk for closing the unit), over a grid of one wave of resident CTAs. A row may be cut into at most
+// U_MAXPARTS units; a vocabulary too long for that has no plan (the full-row kernel takes the batch).
+bool pass_plan(int64_t n_rows, int64_t vocab, int es, PassPlan* out) {
+  if (n_rows <= 0 || vocab <= 0) return false;
+  const int64_t epv = 16 / es, cv = CHUNK_BYTES / 16;
+  const int64_t nvec_max = vocab / epv;  // no row has more body vectors
+  const int64_t cap = (int64_t)pass_ctas_per_sm(es) * sm_count();
+  int lo = 1, hi = U_MAXCPU;
+  if (const char* env = getenv("PB_PASS_CPU")) {
+    const int c = atoi(env);
+    if (c >= 1 && c <= U_MAXCPU) lo = hi = c;
+  }
+  double best = 0.0;
+  bool found = false;
+  for (int cpu = hi; cpu >= lo; --cpu) {
+    const int64_t parts = std::max<int64_t>(1, (nvec_max + cpu * cv - 1) / (cpu * cv));
+    if (parts > U_MAXPARTS) continue;
+    const int64_t units = n_rows * parts;
+    const int64_t grid = std::min(units, cap);
+    const int64_t rounds = (units + grid - 1) / grid;
+    const double cost = (double)rounds * (cpu + 0.5);
+    if (!found || cost < best) {
+      best = cost;
+      found = true;
+      out->cpu = cpu;
+      out->parts = (int)parts;
+      out->units = units;
+      out->grid = grid;
+    }
+  }
+  return found;
+}
+
+constexpr int64_t align256(int64_t n) { return (n + 255) & ~(int64_t)255; }
+
+// workspace of pb_sample_ws: per-row unit counters, per-row info, then the unit records
+int64_t ws_bytes_for(int64_t n_rows, const PassPlan& pl) {
+  return align256(n_rows * 4) + align256(n_rows * (int64_t)sizeof(pb_row_info)) + pl.units * record_bytes(U_CAP);
+}
+
+template <typename T>
+int launch_pass(const PassArgs& a, int grid, cudaStream_t stream) {
+  static unsigned long long configured = 0;  // bit d: device d configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  const int smem = PASS_SMEM;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(pass_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return PB_E_DEVICE;
+    configured |= 1ull << dev;
+  }
+  pass_kernel<T><<<(unsigned)grid, NT, smem, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  return PB_OK;
+}
+
+// pass -> full-row kernel on the rows the pass left as PB_ROW_FALLBACK (see pb_sample_ws)
+int run_pass(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
+             const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
+             uint8_t* workspace, const PassPlan& pl, cudaStream_t st) {
+  uint32_t* row_done = reinterpret_cast<uint32_t*>(workspace);
   pb_row_info* info =
-      out_info ? out_info : reinterpret_cast<pb_row_info*>(records + (int64_t)S * n_rows * record_bytes(L_CAP));
-  ScanArgs sa;
-  sa.logits = static_cast<const char*>(logits);
-  sa.n_rows = n_rows;
-  sa.vocab = vocab;
-  sa.row_stride = row_stride;
-  sa.row_index = row_index;
-  sa.params = params;
-  sa.slices = S;
-  sa.records = records;
-  int rc = (dtype == PB_DTYPE_F32)    ? launch_scan<float>(sa, st)
-           : (dtype == PB_DTYPE_BF16) ? launch_scan<__nv_bfloat16>(sa, st)
-                                      : launch_scan<__half>(sa, st);
-  if (rc != PB_OK) return rc;
-  rc = launch_merge(records, S, n_rows, L_CAP, params, out_token, info, st);
+      out_info ? out_info : reinterpret_cast<pb_row_info*>(workspace + align256(n_rows * 4));
+  uint8_t* records = workspace + align256(n_rows * 4) + align256(n_rows * (int64_t)sizeof(pb_row_info));
+  if (cudaMemsetAsync(row_done, 0, (size_t)n_rows * 4, st) != cudaSuccess) return PB_E_LAUNCH;
+  PassArgs pa;
+  pa.logits = static_cast<const char*>(logits);
+  pa.n_rows = n_rows;
+  pa.vocab = vocab;
+  pa.row_stride = row_stride;
+  pa.row_index = row_index;
+  pa.params = params;
+  pa.cpu = pl.cpu;
+  pa.parts = pl.parts;
+  pa.units = pl.units;
+  pa.row_done = row_done;
+  pa.records = records;
+  pa.out_token = out_token;
+  pa.out_info = info;
+  int rc = (dtype == PB_DTYPE_F32)    ? launch_pass<float>(pa, (int)pl.grid, st)
+           : (dtype == PB_DTYPE_BF16) ? launch_pass<__nv_bfloat16>(pa, (int)pl.grid, st)
+                                      : launch_pass<__half>(pa, (int)pl.grid, st);
   if (rc != PB_OK) return rc;
   Args a;
   a.logits = static_cast<const char*>(logits);
@@ -2451,7 +2789,9 @@ int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap,
 int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype) {
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
-  return ws_bytes_for(n_rows, slices_for(n_rows, vocab, es));
+  PassPlan pl;
+  if (!pass_plan(n_rows, vocab, es, &pl)) return 256;  // such a batch runs the full-row kernel
+  return ws_bytes_for(n_rows, pl);
 }
 
 int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
@@ -2469,10 +2809,13 @@ int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, i
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
-  const int S = slices_for(n_rows, vocab, es);
-  if (ws_bytes < ws_bytes_for(n_rows, S)) return PB_E_INVALID;
-  return run_split(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
-                   static_cast<uint8_t*>(workspace), S, static_cast<cudaStream_t>(stream));
+  PassPlan pl;
+  if (!pass_plan(n_rows, vocab, es, &pl))
+    return pb_sample(logits, dtype, n_rows, vocab, row_stride, row_index, params, out_token, out_info, nullptr,
+                     stream);
+  if (ws_bytes < ws_bytes_for(n_rows, pl)) return PB_E_INVALID;
+  return run_pass(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
+                  static_cast<uint8_t*>(workspace), pl, static_cast<cudaStream_t>(stream));
 }
 
 int64_t pb_sample_noalloc_max_bytes(void) { return NOALLOC_SCRATCH_BYTES; }
@@ -2488,14 +2831,18 @@ int pb_sample_noalloc(const void* logits, int dtype, int64_t n_rows, int64_t voc
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
-  const int S = slices_for(n_rows, vocab, es);
-  if (ws_bytes_for(n_rows, S) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
+  PassPlan pl;
+  if (!pass_plan(n_rows, vocab, es, &pl))  // the full-row kernel needs no workspace
+    return pb_sample(logits, dtype, n_rows, vocab, row_stride, row_index, params, out_token, out_info, nullptr,
+                     stream);
+  if (ws_bytes_for(n_rows, pl) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
   uint8_t* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != PB_OK) return rc;
-  // every byte the launches read is written earlier in the same call: nothing needs clearing
-  return run_split(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info, scratch, S,
-                   static_cast<cudaStream_t>(stream));
+  // run_pass clears the per-row unit counters (a stream-ordered memset); every other byte the
+  // launches read is written earlier in the same call
+  return run_pass(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info, scratch, pl,
+                  static_cast<cudaStream_t>(stream));
 }
 
 uint32_t pb_key_of(float x) {

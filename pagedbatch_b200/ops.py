@@ -46,9 +46,9 @@ def params_tensor(rec: np.ndarray, device, pinned: bool = True) -> torch.Tensor:
 _WS: dict = {}
 
 
-def _split_path() -> bool:
-    """The single full-row launch (default) or, with PB_PATH=split, scan + merge + fallback launches."""
-    return os.environ.get("PB_PATH", "full") == "split"
+def _pass_path() -> bool:
+    """The single full-row launch (default) or, with PB_PATH=pass, the persistent pass + fallback launches."""
+    return os.environ.get("PB_PATH", "full") == "pass"
 
 
 def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
@@ -90,7 +90,7 @@ def _launch(logits: torch.Tensor, params: torch.Tensor, row_index, with_info: bo
     info = torch.empty((n, _lib.ROW_INFO.itemsize), dtype=torch.uint8, device=dev) if with_info else None
     probs = torch.empty((n, V), dtype=torch.float32, device=dev) if with_probs else None
     L = _lib.load()
-    if not with_probs and _split_path():
+    if not with_probs and _pass_path():
         with torch.cuda.device(dev):
             need = L.pb_sample_ws_bytes(n, V, _DTYPE_CODE[logits.dtype])
             ws = _workspace(dev, need)

@@ -57,7 +57,7 @@ def rec_for(params, uniforms):
 def _need_cuda(cuda):
     yield
     os.environ.pop("PB_CLUSTER", None)
-    os.environ.pop("PB_SLICES", None)
+    os.environ.pop("PB_PASS_CPU", None)
     os.environ.pop("PB_PATH", None)
 
 
@@ -302,12 +302,12 @@ def test_vocab_parallel_api_one_rank_nccl():
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("slices", ["1", "2", "4", "8"])
-def test_split_path_modes_and_edges(slices):
-    """The scan + merge + fallback launches (pb_sample_ws) against the oracle, every slice count."""
-    os.environ["PB_PATH"] = "split"
-    os.environ["PB_SLICES"] = slices
-    rng = np.random.default_rng(20 + int(slices))
+@pytest.mark.parametrize("cpu", ["1", "2", "4", "8"])
+def test_pass_path_modes_and_edges(cpu):
+    """The persistent pass + fallback launches (pb_sample_ws) against the oracle, several unit sizes."""
+    os.environ["PB_PATH"] = "pass"
+    os.environ["PB_PASS_CPU"] = cpu
+    rng = np.random.default_rng(20 + int(cpu))
     for V in (1, 3, 17, 258, 4099, 49152, 128256):
         B = 24
         x = workloads.head_boosted(B, V, seed=V)
@@ -316,7 +316,7 @@ def test_split_path_modes_and_edges(slices):
         p = rng.choice([1.0, 0.5, 0.9, 0.99, 1e-6], B)
         u = rng.random(B)
         u[:2] = [0.0, np.nextafter(1.0, 0.0)]
-        compare(x, oracle.make_params(t, p, k, u), probs=False, label=f"split S={slices} V={V}")
+        compare(x, oracle.make_params(t, p, k, u), probs=False, label=f"pass cpu={cpu} V={V}")
     x = torch.randn(7, 600)
     x[0, 5] = float("nan")
     x[1, 7] = float("inf")
@@ -326,27 +326,39 @@ def test_split_path_modes_and_edges(slices):
     x[6, 100:] = float("-inf")
     rec = oracle.make_params([1.0, 1.0, 1.0, 1.0, 0.0, 1.0, 0.0], [1.0] * 7, [10, 10, 10, 10, 0, 10, 0], [0.5] * 7)
     rec["uniform"][5] = 1.0
-    compare(x, rec, probs=False, label=f"split nonfinite S={slices}")
+    compare(x, rec, probs=False, label=f"pass nonfinite cpu={cpu}")
     x2 = torch.tensor([[1.0, float("nan"), 3.0, float("nan")], [float("-inf")] * 4, [-0.0, 0.0, -1.0, 0.0]])
-    compare(x2, oracle.make_params([0.0] * 3, [1.0] * 3, [0] * 3, [0.0] * 3), probs=False, label="split greedy edge")
+    compare(x2, oracle.make_params([0.0] * 3, [1.0] * 3, [0] * 3, [0.0] * 3), probs=False, label="pass greedy edge")
     rec = oracle.make_params([-1.0, 1.0, 1.0, float("nan")], [1.0, 0.0, 1.5, 1.0], [0, 0, 0, 0], [0.5] * 4)
-    compare(torch.randn(4, 100), rec, probs=False, label="split bad params")
+    compare(torch.randn(4, 100), rec, probs=False, label="pass bad params")
 
 
-def test_split_path_configs_and_row_index():
-    os.environ["PB_PATH"] = "split"
+def test_pass_path_configs_and_row_index():
+    os.environ["PB_PATH"] = "pass"
     for w in (workloads.config0(), workloads.config1(), workloads.config2()):
-        compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label=f"split {w.name}")
+        compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label=f"pass {w.name}")
+    # many units per CTA: each CTA walks a dozen or more units and merges several rows
+    for B, V in ((400, 128256), (3000, 4099)):
+        rng = np.random.default_rng(B)
+        x = workloads.head_boosted(B, V, seed=B)
+        t = rng.choice([0.0, 0.7, 1.0], B)
+        k = rng.choice([1, 20, 50, 256, 257], B)
+        p = rng.choice([1.0, 0.9, 0.95], B)
+        compare(x, oracle.make_params(t, p, k, rng.random(B)), probs=False, label=f"pass B={B} V={V}")
+    # rising values: the first chunk's threshold admits every later value, units overflow and the
+    # rows fall back to the full-row kernel
+    x = torch.arange(6 * 70000, dtype=torch.float32).reshape(6, 70000) % 70001
+    compare(x, oracle.make_params([1.0] * 6, [0.9] * 6, [50] * 6, [0.3] * 6), probs=False, label="pass rising")
     w = workloads.config1(rows=32)
     sel = np.array([31, 0, 5, 5, 17, 2, 30], np.int32)
     rec = rec_for([w.params[i] for i in sel], [w.uniforms()[i] for i in sel])
-    compare(w.logits, rec, sel, probs=False, label="split row_index")
+    compare(w.logits, rec, sel, probs=False, label="pass row_index")
     os.environ.pop("PB_PATH")
     compare(w.logits, rec, sel, probs=False, label="full row_index")
 
 
-def test_split_path_ties_and_sparse_rows():
-    os.environ["PB_PATH"] = "split"
+def test_pass_path_ties_and_sparse_rows():
+    os.environ["PB_PATH"] = "pass"
     V = 20000
     x = torch.zeros(6, V)
     x[1, ::3] = 1.0
@@ -356,16 +368,16 @@ def test_split_path_ties_and_sparse_rows():
     x[5, :] = -1.0
     rng = np.random.default_rng(13)
     for t, k, p in [(0.5, 500, 1.0), (1.0, 7, 0.99), (0.0, 0, 1.0), (1.0, 1, 1.0), (1.0, 300, 0.3)]:
-        for sl in ("1", "4"):
-            os.environ["PB_SLICES"] = sl
+        for cpu in ("1", "4"):
+            os.environ["PB_PASS_CPU"] = cpu
             compare(x, oracle.make_params([t] * 6, [p] * 6, [k] * 6, rng.random(6)), probs=False,
-                    label=f"split ties t={t} k={k} S={sl}")
+                    label=f"pass ties t={t} k={k} cpu={cpu}")
     V = 4099
     x = torch.full((4, V), float("-inf"))
     for r, n in enumerate((1, 37, 500, 999)):
         cols = torch.from_numpy(rng.choice(V, n, replace=False))
         x[r, cols] = torch.randn(n, generator=torch.Generator().manual_seed(r)) * 2.0
     rec = oracle.make_params([1.0, 0.7, 1.0, 1.3], [1.0, 0.9, 1.0, 0.5], [400, 400, 400, 400], rng.random(4))
-    for sl in ("1", "8"):
-        os.environ["PB_SLICES"] = sl
-        compare(x, rec, probs=False, label=f"split sparse-finite S={sl}")
+    for cpu in ("1", "8"):
+        os.environ["PB_PASS_CPU"] = cpu
+        compare(x, rec, probs=False, label=f"pass sparse-finite cpu={cpu}")
