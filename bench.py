@@ -378,6 +378,55 @@ def load_traffic(workload):
         return None
 
 
+def run_calibration(args):
+    """Plain torch reductions over the same logits, timed like the sampler (rotating input copies,
+    one CUDA graph of K launches between CUDA events): what one read-once pass over this tensor
+    costs at this size on this GPU, beside the sampler itself. One JSON line, 1 GPU."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = make_workload(args.workload, 0)
+    rec = sampling.pack_rows(w.params, np.array(w.uniforms()))
+    params = ops.params_tensor(rec, dev)
+    bufs = [w.logits.to(dev) for _ in range(NROT)]
+    nbytes = w.logits.numel() * w.logits.element_size()
+    stream = torch.cuda.Stream(dev)
+
+    def graph_us(f):
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                f(bufs[i % NROT])
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(args.steps):
+                f(bufs[i % NROT])
+        g.replay()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            with torch.cuda.stream(stream):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1) * 1e3 / args.steps)
+        us = sorted(times)[2]
+        return {"us_per_launch": us, "read_GBps": nbytes / (us * 1e-6) / 1e9}
+
+    line = {
+        "calibration": w.name,
+        "bytes_per_launch": nbytes,
+        "timing": "CUDA graph of K launches between CUDA events, median of 5 replays; "
+                  f"{NROT} rotating input copies",
+        "torch_sum": graph_us(lambda a: a.sum()),
+        "torch_amax_rows": graph_us(lambda a: torch.amax(a, dim=1)),
+        "torch_max_argmax_rows": graph_us(lambda a: torch.max(a, dim=1)),
+        "pb_sample": graph_us(lambda a: ops.sample_op(a, params)),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -387,10 +436,14 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=["cfg0", "cfg1", "cfg2", "cfg2flat", "cfg3"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="eager launches only (for ncu), no timing")
+    ap.add_argument("--calibrate", action="store_true",
+                    help="time plain torch reductions over the same logits beside the sampler (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.calibrate:
+        run_calibration(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "cfg3":
         run_vocab_parallel(args)

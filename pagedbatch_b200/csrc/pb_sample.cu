@@ -44,7 +44,7 @@ constexpr int RING_BYTES = 65536;
 constexpr int MAX_STAGE = 16;
 constexpr int CAND_CAP = 4096;      // candidate entries per CTA
 constexpr int SLOTS = CAND_CAP / NT; // candidate slots per thread
-constexpr int CP_CHUNKS = 8;        // chunks between CTA checkpoints (a multiple of the ring depth)
+constexpr int CP_CHUNKS = 8;        // chunks between CTA checkpoints (rows with a small top_k)
 constexpr uint32_t BUCKET = 32;     // keys left between the bisection bounds when it stops early
 constexpr int KSMALL = 1024;        // largest top_k resolved from the streamed candidates
 constexpr int KCAP = 2048;          // survivors of the small path sorted in rank 0
@@ -711,15 +711,24 @@ __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank,
   if (tid == 0) sh.thr_f = tie_floor(value_of(kth_raw), tf);
   __syncthreads();
   const uint32_t fk = key_of(sh.thr_f);
-  int w = 0;
+  // A large k keeps about k candidates, and a thread may hold many of them: deal the kept ones out
+  // evenly (entry i of the dense list goes to slot i / NT of thread i % NT), so that no thread
+  // stays crowded with candidates the new threshold cannot drop.
+  uint64_t v[SLOTS];
+  uint32_t keep = 0;
 #pragma unroll
   for (int j = 0; j < SLOTS; ++j) {
-    if (j < nc && kk[j] >= fk) {
-      candB[w * NT + tid] = candB[j * NT + tid];
-      ++w;
-    }
+    v[j] = (j < nc) ? candB[j * NT + tid] : 0ull;
+    keep += (j < nc && kk[j] >= fk) ? 1u : 0u;
   }
-  return w;
+  uint32_t kept;
+  uint32_t pos = block_excl_scan<uint32_t, NT>(keep, sh.s32, &kept);  // every slot is read first
+#pragma unroll
+  for (int j = 0; j < SLOTS; ++j) {
+    if (j < nc && kk[j] >= fk) candB[pos++] = v[j];
+  }
+  __syncthreads();
+  return (kept > (uint32_t)tid) ? (int)((kept - (uint32_t)tid + NT - 1) / NT) : 0;
 }
 
 // First candidate threshold: sh.thr_f = the tie floor of the top_k-th largest value among the nv
@@ -976,6 +985,9 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     }
     bool cta_timeout = false;
     int cp = 0;              // checkpoints passed
+    // A large k passes about k values per chunk past a threshold taken from the first chunk, so the
+    // slots fill within a few chunks: such rows meet (and may compact) after every chunk.
+    const int cp_every = (filtering && top_k > OFFER_PREFER) ? 1 : CP_CHUNKS;
     // 32-bit chunk and vector counters: a slice holds fewer than 2^24 elements
     const int nch = (int)nchunks, nvec32 = (int)s.nvec;
     const uint32_t e_base = (uint32_t)s.vec_e0 + (uint32_t)tid * EPV;  // element of vector tid of chunk 0
@@ -1050,7 +1062,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           }
         }
       }
-      if (c % CP_CHUNKS == CP_CHUNKS - 1 || c == nch - 1) {
+      if ((c + 1) % cp_every == 0 || c == nch - 1) {
         // checkpoint; flag and count words rotate over three slots so a reset never races a write
         const int mine = (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && nc >= SLOTS / 2) ? 1 : 0);
         if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
