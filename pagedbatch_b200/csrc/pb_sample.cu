@@ -875,6 +875,11 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
   const int rank = (int)cluster.block_rank();
+  // cluster barrier; a one-CTA cluster needs only the CTA barrier (same ordering, far cheaper)
+  auto csync = [&]() {
+    if (C == 1) __syncthreads();
+    else cluster.sync();
+  };
   const int64_t item = blockIdx.x / C;
   const int tid = threadIdx.x;
   const int64_t V = a.vocab;
@@ -1166,7 +1171,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       sh.pub_timeout = sh.timeout;
     }
   }
-  cluster.sync();  // S1: stage-1 results visible cluster-wide
+  csync();  // S1: stage-1 results visible cluster-wide
 
   if (tid == 0) {
     float bv = -INFINITY, rm = -INFINITY, mn = INFINITY;
@@ -1223,7 +1228,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         if (x != x) atomicMin(&sh.nan_idx, e);
       });
       __syncthreads();
-      cluster.sync();
+      csync();
       if (tid == 0) {
         uint32_t ni = 0xFFFFFFFFu;
         for (int r = 0; r < C; ++r) ni = min(ni, cluster.map_shared_rank(&sh, r)->nan_idx);
@@ -1237,7 +1242,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     info.kept_count = 1;
     info.flags = PB_PATH_GREEDY;
     zero_probs();
-    cluster.sync();
+    csync();
     if (prow && rank == 0 && tid == 0) prow[token] = 1.0f;
     finished = true;
   } else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) {
@@ -1343,7 +1348,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       }
       __syncthreads();
     }
-    cluster.sync();  // S2: rank 0 finished (or gave up); peers' zero-fill done
+    csync();  // S2: rank 0 finished (or gave up); peers' zero-fill done
     pull_dec(cluster, sh);
     if (sh.dec_local.action == ACT_DONE) {
       if (rank == 0 && prow) {
@@ -1356,7 +1361,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       }
       finished = true;
     }
-    cluster.sync();  // rank 0's gather/candidate buffers are free again
+    csync();  // rank 0's gather/candidate buffers are free again
   }
 
   // ---------------- large path: cooperative histogram selection ----------------
@@ -1375,7 +1380,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         if (d.action == ACT_DONE) break;
         if (d.action == ACT_GATHER) {
           if (rank == 0 && tid == 0) sh.g_n = 0;
-          cluster.sync();
+          csync();
           int32_t* gn = cluster.map_shared_rank(&sh.g_n, 0);
           uint64_t* g0 = cluster.map_shared_rank(G, 0);
           for_slice<T>(row, s, [&](float x, uint32_t e) {
@@ -1385,7 +1390,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             const int pos = atomicAdd(gn, 1);
             if (pos < GCAP) g0[pos] = compose(k, e);
           });
-          cluster.sync();
+          csync();
           if (rank == 0) {
             const int n = min(sh.g_n, GCAP);
             block_sort_desc(G, n);
@@ -1419,7 +1424,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             }
             __syncthreads();
           }
-          cluster.sync();
+          csync();
           pull_dec(cluster, sh);
           continue;
         }
@@ -1439,7 +1444,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             });
             cnt = warp_sum(cnt);
             if ((tid & 31) == 0 && cnt) atomicAdd(&sh.nk, (int)cnt);
-            cluster.sync();
+            csync();
             uint64_t before = 0;
             for (int r = 0; r < rank; ++r) before += (uint64_t)cluster.map_shared_rank(&sh, r)->nk;
             const uint64_t mine = (uint64_t)sh.nk;
@@ -1454,7 +1459,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
                   });
             }
           }
-          cluster.sync();
+          csync();
           if (rank == 0 && tid == 0) {
             Dec r = d;
             r.action = ACT_DONE;
@@ -1468,7 +1473,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             if (need_index && sh.g_n < 0) r.fail = 1;
             sh.dec = r;
           }
-          cluster.sync();
+          csync();
           pull_dec(cluster, sh);
           continue;
         }
@@ -1489,7 +1494,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           }
           atomicAdd(&hc[(d.hi - k) >> shift], 1u);
         });
-        cluster.sync();
+        csync();
         if (rank == 0) {
           int b;
           uint64_t aw = 0, ac = 0, bw = 0, bc = 0;
@@ -1525,14 +1530,14 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           }
           __syncthreads();
         }
-        cluster.sync();
+        csync();
         pull_dec(cluster, sh);
       }
       if (sh.dec_local.action != ACT_DONE || sh.dec_local.fail) failed = true;
     };
 
     // Level-1 decision from the reduced histogram h1q/h1c (rank 0 threads only). The caller
-    // brackets it with cluster.sync() so that no peer still reads the previous decision.
+    // brackets it with cluster barriers so that no peer still reads the previous decision.
     auto level1 = [&](int mode, float scale, uint64_t target) {
       if (tid == 0) {
         Dec r = {};
@@ -1601,7 +1606,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         }
         atomicAdd(&hc[b], 1u);
       });
-      cluster.sync();
+      csync();
       if (rank == 0) {
         for (int b = tid; b < NBIN; b += NT) {
           uint64_t q = 0;
@@ -1629,11 +1634,11 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     if (topk_active) {
       level1_pass(MODE_COUNT, 0, scale_all);
       if (rank == 0) level1(MODE_COUNT, scale_all, (uint64_t)(top_k - 1));
-      cluster.sync();
+      csync();
       pull_dec(cluster, sh);
       select(MODE_COUNT, 0, (uint64_t)(top_k - 1), false);
       kfloor = sh.dec_local.res_key;
-      cluster.sync();
+      csync();
     }
 
     // (b) pass Z: weight mass by level-1 bin over the survivors K = {key >= kfloor}
@@ -1646,10 +1651,10 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       if (tid == 0) sh.dec.aux = tot;
       __syncthreads();
     }
-    cluster.sync();
+    csync();
     pull_dec(cluster, sh);
     const uint64_t zq = sh.dec_local.aux;
-    cluster.sync();
+    csync();
 
     // (c) top-p cut: the last kept position is the element whose inclusive mass first exceeds tp
     uint32_t cut_key = 0;
@@ -1658,7 +1663,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     if (cut) {
       const uint64_t tp = mul_floor(pf, zq);
       if (rank == 0) level1(MODE_MASS, scale_mass, tp);
-      cluster.sync();
+      csync();
       pull_dec(cluster, sh);
       select(MODE_MASS, kfloor, tp, false);
       const Dec r = sh.dec_local;
@@ -1670,18 +1675,18 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       } else {
         failed = true;
       }
-      cluster.sync();
+      csync();
     }
 
     // (d) the draw over the kept prefix (t < kept, so it never reaches past the cut)
     if (!failed) {
       const uint64_t t = scale_u53(u53, kept);
       if (rank == 0) level1(MODE_MASS, scale_mass, t);
-      cluster.sync();
+      csync();
       pull_dec(cluster, sh);
       select(MODE_MASS, kfloor, t, true);
       token = sh.dec_local.res_idx;
-      cluster.sync();
+      csync();
     }
     if (failed) info.status = PB_ROW_INTERNAL;
     info.z_q = zq;
@@ -1700,7 +1705,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         });
       cnt = warp_sum(cnt);
       if ((tid & 31) == 0 && cnt) atomicAdd(&sh.nk, (int)cnt);
-      cluster.sync();
+      csync();
       uint64_t before = 0;
       for (int r = 0; r < rank; ++r) before += (uint64_t)cluster.map_shared_rank(&sh, r)->nk;
       uint32_t kc = 0, kmin_kept = 0xFFFFFFFFu, kmin_cnt = 0;
@@ -1762,7 +1767,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         sh.pub_idx = C0;
         sh.pub_min = T0;
       }
-      cluster.sync();
+      csync();
       if (rank == 0 && tid == 0) {
         uint32_t K0 = 0xFFFFFFFFu, C0 = 0, T0 = 0;
         for (int r = 0; r < C; ++r) {
@@ -1813,7 +1818,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       o->kept_q = info.kept_q;
     }
   }
-  cluster.sync();  // no CTA leaves while another may still read its shared memory
+  csync();  // no CTA leaves while another may still read its shared memory
 }
 
 // ---- vocabulary-parallel merge -----------------------------------------------------------
