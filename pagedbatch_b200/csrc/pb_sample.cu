@@ -39,12 +39,13 @@ namespace {
 
 constexpr int NT = 256;             // threads per CTA
 constexpr int NW = NT / 32;
-constexpr int CHUNK_BYTES = 16384;  // bytes per staged chunk
+constexpr int CHUNK_BYTES = 32768;  // bytes per staged chunk (the ring holds two: a warp's fixed cost per
+                                    // chunk, wait and release, is paid once per 32 KB)
 constexpr int RING_BYTES = 65536;
 constexpr int MAX_STAGE = 16;
 constexpr int CAND_CAP = 4096;      // candidate entries per CTA
 constexpr int SLOTS = CAND_CAP / NT; // candidate slots per thread
-constexpr int CP_CHUNKS = 8;        // chunks between CTA checkpoints (rows with a small top_k)
+constexpr int CP_CHUNKS = 4;        // chunks between CTA checkpoints (128 KB; rows with a small top_k)
 constexpr uint32_t BUCKET = 32;     // keys left between the bisection bounds when it stops early
 constexpr int KSMALL = 1024;        // largest top_k resolved from the streamed candidates
 constexpr int KCAP = 2048;          // survivors of the small path sorted in rank 0
@@ -120,6 +121,7 @@ struct Shared {
   int64_t row;
   // stage-1 state
   int32_t cand_n, overflow, timeout;
+  uint32_t app_n;  // entries of the dense candidate list (rows with a large top_k)
   uint32_t thr;
   float thr_f;
   // published per-CTA stage-1 results (read by the other CTAs of the cluster)
@@ -661,13 +663,38 @@ __device__ uint32_t block_offer_bound(uint32_t key, int k, Shared& sh) {
   return mn;
 }
 
+// Warp-aggregated append of a candidate (raw value x, index e) to the CTA's dense candidate list
+// (entry i sits in slot i / NT of thread i % NT, the layout compact_slots repacks to). All 32 lanes
+// call. Returns false for a lane whose candidate found no room.
+__device__ __forceinline__ bool append_dense(bool pass, float x, uint32_t e, uint64_t* list, uint32_t* cnt) {
+  const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
+  if (m == 0) return true;
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(m) - 1;
+  uint32_t base = 0;
+  if (lane == leader) base = atomicAdd(cnt, (uint32_t)__popc(m));
+  base = __shfl_sync(0xFFFFFFFFu, base, leader);
+  if (!pass) return true;
+  const uint32_t pos = base + (uint32_t)__popc(m & lanemask_lt());
+  if (pos >= (uint32_t)CAND_CAP) return false;
+  list[pos] = compose(key_of(x), e);
+  return true;
+}
+
+// slots a thread holds of a dense list of n entries
+__device__ __forceinline__ int dense_slots(uint32_t n) {
+  const uint32_t t = threadIdx.x;
+  return (n > t) ? (int)min((uint32_t)SLOTS, (n - t + NT - 1) / NT) : 0;
+}
+
 // ---- the kernel -------------------------------------------------------------------------
 
 // Raise the candidate threshold sh.thr_f to the tie floor of a lower bound of the kth_rank-th
 // largest candidate held in the per-thread slots (slot j of thread t at candB[j * NT + t]) and
 // drop the candidates below it. Returns this thread's new slot count. All threads call; a barrier
 // separates two calls. Kept out of line so the streaming loop stays small.
-__device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank, float tf, Shared& sh) {
+__device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank, float tf, Shared& sh,
+                                         uint32_t* count_out = nullptr) {
   const int tid = threadIdx.x;
   if (kth_rank <= OFFER_PREFER) {
     // every thread offers its largest candidate; the bound only ever raises the threshold
@@ -727,6 +754,7 @@ __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank,
   for (int j = 0; j < SLOTS; ++j) {
     if (j < nc && kk[j] >= fk) candB[pos++] = v[j];
   }
+  if (count_out && tid == 0) *count_out = kept;
   __syncthreads();
   return (kept > (uint32_t)tid) ? (int)((kept - (uint32_t)tid + NT - 1) / NT) : 0;
 }
@@ -897,6 +925,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     sh.filtering = !sh.greedy && p.top_k > 0 && (int64_t)p.top_k < V && p.top_k <= KSMALL;
     sh.row = a.row_index ? (int64_t)a.row_index[item] : item;
     sh.cand_n = 0;
+    sh.app_n = 0;
     sh.overflow = 0;
     sh.timeout = 0;
     sh.thr = 0;
@@ -930,7 +959,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   // Raw values are compared directly (x / T is monotone in x for T > 0): a NaN-propagating max,
   // the first (lowest-index) maximum, the smallest value above -inf for rows that need it, and for
   // small top-k rows the candidates (raw value >= a running threshold) in per-thread slots.
-  // Each thread handles VPT independent 16-byte vectors per 16 KB chunk.
+  // Each thread handles VPT independent 16-byte vectors per 32 KB chunk.
   const bool track_min = !greedy && !filtering;  // rows that take the cooperative path
   float runmax = -INFINITY, bestv = -INFINITY, mnv = INFINITY;
   uint32_t bidx = 0xFFFFFFFFu;
@@ -949,7 +978,12 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   // Raise the threshold to the tie floor of the kth_rank-th largest candidate and drop the
   // candidates below it (each thread compacts its own slots). All threads call; a barrier
   // separates two calls.
-  auto compact = [&](int kth_rank) { nc = compact_slots(candB, nc, kth_rank, tf, sh); };
+  // Rows with a large top_k pass about k values per chunk and keep about k: their candidates go to
+  // one dense list of the CTA (warp-aggregated appends), so no thread's slots overflow first.
+  const bool dense_mode = filtering && top_k > OFFER_PREFER;
+  auto compact = [&](int kth_rank) {
+    nc = compact_slots(candB, nc, kth_rank, tf, sh, dense_mode ? &sh.app_n : nullptr);
+  };
   auto visit1 = [&](float x, uint32_t e) {
     runmax = fmax_nan(runmax, x);
     if (x > bestv) {
@@ -1056,7 +1090,18 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           for (int q = 0; q < EPV; ++q)
             if (x[j][q] > -INFINITY) mnv = fminf(mnv, x[j][q]);
       }
-      if (filtering && !row_ovf) {
+      if (filtering && !row_ovf && dense_mode) {
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const bool any = j * NT + tid < nv && vm[j] >= t;
+          if (__any_sync(0xFFFFFFFFu, any)) {
+            const uint32_t e0 = e_base + (uint32_t)((c * CHUNK_VEC + j * NT) * EPV);
+#pragma unroll
+            for (int q = 0; q < EPV; ++q)
+              if (!append_dense(any && x[j][q] >= t, x[j][q], e0 + q, candB, &sh.app_n)) ovf = true;
+          }
+        }
+      } else if (filtering && !row_ovf) {
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
           if (j * NT + tid < nv && vm[j] >= t) {  // vectors past the chunk's end hold -inf padding
@@ -1069,15 +1114,18 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       }
       if ((c + 1) % cp_every == 0 || c == nch - 1) {
         // checkpoint; flag and count words rotate over three slots so a reset never races a write
-        const int mine = (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && nc >= SLOTS / 2) ? 1 : 0);
+        const int mine =
+            (timed_out ? 4 : 0) | (ovf ? 2 : 0) | ((filtering && !dense_mode && nc >= SLOTS / 2) ? 1 : 0);
         if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
-        if (filtering) {
+        if (filtering && !dense_mode) {
           const uint32_t wsum = __reduce_add_sync(0xFFFFFFFFu, (uint32_t)nc);
           if (lane == 0 && wsum) atomicAdd(&sh.cp_count[cp % 3], wsum);
         }
         __syncthreads();
         const int f = sh.cp_flags[cp % 3];
-        const uint32_t held = sh.cp_count[cp % 3];
+        const uint32_t held = dense_mode ? sh.app_n : sh.cp_count[cp % 3];
+        // every thread reads the dense count before any warp appends again (one decision per CTA)
+        if (dense_mode) __syncthreads();
         if (tid == 0) {
           sh.cp_flags[(cp + 2) % 3] = 0;
           sh.cp_count[(cp + 2) % 3] = 0;
@@ -1090,7 +1138,10 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         if (f & 2) row_ovf = true;
         // raise the threshold once the CTA holds a few times k candidates, so it keeps tracking
         // the k-th of everything seen (the pass rate then falls with the chunks streamed)
-        if (((f & 1) || held >= (uint32_t)(4 * top_k + 64)) && !row_ovf) compact(top_k);
+        if (((f & 1) || held >= (uint32_t)((dense_mode ? 2 : 4) * top_k + 64)) && !row_ovf) {
+          if (dense_mode) nc = dense_slots(held);  // no overflow: held <= CAND_CAP
+          compact(top_k);
+        }
         t = sh.thr_f;  // every thread passed the barrier after any write of the threshold
       }
     }
@@ -1111,16 +1162,32 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     // head and tail elements against the final threshold
     __syncthreads();
     const float t = sh.thr_f;
-    for (int64_t e = tid; e < s.head_n; e += NT) {
-      const float x = Elem<T>::ld(row + e);
-      if (x >= t) push(x, (uint32_t)e);
-    }
-    for (int64_t e = tid; e < s.tail_n; e += NT) {
-      const float x = Elem<T>::ld(row + s.tail_e0 + e);
-      if (x >= t) push(x, (uint32_t)(s.tail_e0 + e));
+    if (dense_mode) {
+      // every lane of a warp takes part in each append
+      for (int64_t e0 = 0; e0 < s.head_n; e0 += NT) {
+        const int64_t e = e0 + tid;
+        const float x = (e < s.head_n) ? Elem<T>::ld(row + e) : -INFINITY;
+        if (!append_dense(!row_ovf && e < s.head_n && x >= t, x, (uint32_t)e, candB, &sh.app_n)) ovf = true;
+      }
+      for (int64_t e0 = 0; e0 < s.tail_n; e0 += NT) {
+        const int64_t e = e0 + tid;
+        const float x = (e < s.tail_n) ? Elem<T>::ld(row + s.tail_e0 + e) : -INFINITY;
+        if (!append_dense(!row_ovf && e < s.tail_n && x >= t, x, (uint32_t)(s.tail_e0 + e), candB, &sh.app_n))
+          ovf = true;
+      }
+    } else {
+      for (int64_t e = tid; e < s.head_n; e += NT) {
+        const float x = Elem<T>::ld(row + e);
+        if (x >= t) push(x, (uint32_t)e);
+      }
+      for (int64_t e = tid; e < s.tail_n; e += NT) {
+        const float x = Elem<T>::ld(row + s.tail_e0 + e);
+        if (x >= t) push(x, (uint32_t)(s.tail_e0 + e));
+      }
     }
     if (__syncthreads_or(ovf)) row_ovf = true;
     if (!row_ovf) {
+      if (dense_mode) nc = dense_slots(sh.app_n);
       // shrink the list to this slice's top_k (plus ties), then pack it densely into the idle ring
       compact(top_k);
       uint32_t tot;
