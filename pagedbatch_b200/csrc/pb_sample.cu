@@ -547,6 +547,14 @@ __device__ float tie_floor(float t, float tf) {
   return -INFINITY;
 }
 
+// 1 / t when t is a power of two whose reciprocal is a normal float (then exact), else 0
+__device__ __forceinline__ float exact_reciprocal(float t) {
+  const uint32_t b = __float_as_uint(t);
+  const uint32_t e = (b >> 23) & 0xFF;
+  if ((b & 0x807FFFFFu) != 0 || e < 1 || e > 253) return 0.0f;
+  return __uint_as_float((254u - e) << 23);
+}
+
 // level-1 bin of a key: distance below the max, scaled; non-increasing in the key
 __device__ __forceinline__ int bin_of(float key, float m, float scale) {
   const float v = __fmul_rn(-__fsub_rn(key, m), scale);
@@ -951,6 +959,11 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   const bool greedy = sh.greedy;
   const bool filtering = sh.filtering;
   const float tf = sh.tf;
+  // x / T per element (the cooperative path's passes): a power-of-two T has an exact reciprocal,
+  // and then x * (1 / T) rounds the same real number as x / T, so it is the same float for a
+  // fraction of the cost
+  const float t_inv = exact_reciprocal(tf);
+  auto scaled = [&](float x) { return (t_inv != 0.0f) ? __fmul_rn(x, t_inv) : __fdiv_rn(x, tf); };
   const int32_t top_k = sh.top_k;
   const T* row = reinterpret_cast<const T*>(a.logits) + sh.row * a.row_stride;
   const Slice s = make_slice(row, V, rank, C);
@@ -1451,7 +1464,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
           int32_t* gn = cluster.map_shared_rank(&sh.g_n, 0);
           uint64_t* g0 = cluster.map_shared_rank(G, 0);
           for_slice<T>(row, s, [&](float x, uint32_t e) {
-            const uint32_t k = key_of(__fdiv_rn(x, tf));
+            const uint32_t k = key_of(scaled(x));
             if (k < d.lo || k > d.hi || k < kfloor) return;
             if (mode == MODE_MASS && weight_q(value_of(k), m) == 0) return;
             const int pos = atomicAdd(gn, 1);
@@ -1507,7 +1520,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
             __syncthreads();
             uint32_t cnt = 0;
             for_slice<T>(row, s, [&](float x, uint32_t) {
-              if (key_of(__fdiv_rn(x, tf)) == d.lo) cnt++;
+              if (key_of(scaled(x)) == d.lo) cnt++;
             });
             cnt = warp_sum(cnt);
             if ((tid & 31) == 0 && cnt) atomicAdd(&sh.nk, (int)cnt);
@@ -1520,7 +1533,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
               const uint32_t want = (uint32_t)(skip - before);
               int32_t* gidx = cluster.map_shared_rank(&sh.g_n, 0);
               ordered_slice<T>(
-                  row, s, sh, [&](float x, uint32_t) { return key_of(__fdiv_rn(x, tf)) == d.lo; },
+                  row, s, sh, [&](float x, uint32_t) { return key_of(scaled(x)) == d.lo; },
                   [&](float, uint32_t e, uint32_t rnk) {
                     if (rnk == want) *gidx = (int32_t)e;
                   });
@@ -1552,7 +1565,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
         }
         __syncthreads();
         for_slice<T>(row, s, [&](float x, uint32_t) {
-          const uint32_t k = key_of(__fdiv_rn(x, tf));
+          const uint32_t k = key_of(scaled(x));
           if (k < d.lo || k > d.hi || k < kfloor) return;
           if (mode == MODE_MASS) {
             const uint64_t wq = weight_q(value_of(k), m);
@@ -1662,7 +1675,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       }
       __syncthreads();
       for_slice<T>(row, s, [&](float x, uint32_t) {
-        const uint32_t k = key_of(__fdiv_rn(x, tf));
+        const uint32_t k = key_of(scaled(x));
         if (k < kfloor) return;
         const float y = value_of(k);
         const int b = bin_of(y, m, scale);
@@ -1691,9 +1704,11 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
 
     const float kmin_v = (sh.row_mnv < INFINITY) ? __fdiv_rn(sh.row_mnv, tf) : m;
     const float range_all = __fsub_rn(m, kmin_v);
-    const float scale_all = (range_all > 0.0f) ? __fdiv_rn((float)NBIN, range_all) : 0.0f;
+    // (a range below NBIN / FLT_MAX would make the scale infinite and the max's bin 0 * inf = NaN:
+    // the largest finite scale keeps the bins monotone in the key)
+    const float scale_all = (range_all > 0.0f) ? fminf(__fdiv_rn((float)NBIN, range_all), 0x1.fffffep127f) : 0.0f;
     const float range_mass = fminf(range_all, MASS_RANGE);
-    const float scale_mass = (range_mass > 0.0f) ? __fdiv_rn((float)NBIN, range_mass) : 0.0f;
+    const float scale_mass = (range_mass > 0.0f) ? fminf(__fdiv_rn((float)NBIN, range_mass), 0x1.fffffep127f) : 0.0f;
 
     // (a) top-k over the whole row when the streamed candidates could not settle it
     uint32_t kfloor = 0;
@@ -1768,7 +1783,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       uint32_t cnt = 0;
       if (cut)
         for_slice<T>(row, s, [&](float x, uint32_t) {
-          if (key_of(__fdiv_rn(x, tf)) == cut_key) cnt++;
+          if (key_of(scaled(x)) == cut_key) cnt++;
         });
       cnt = warp_sum(cnt);
       if ((tid & 31) == 0 && cnt) atomicAdd(&sh.nk, (int)cnt);
@@ -1777,7 +1792,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       for (int r = 0; r < rank; ++r) before += (uint64_t)cluster.map_shared_rank(&sh, r)->nk;
       uint32_t kc = 0, kmin_kept = 0xFFFFFFFFu, kmin_cnt = 0;
       for_slice<T>(row, s, [&](float x, uint32_t e) {
-        const uint32_t k = key_of(__fdiv_rn(x, tf));
+        const uint32_t k = key_of(scaled(x));
         if (cut && k == cut_key) return;  // settled in index order below
         const bool keep = k >= kfloor && !(cut && k < cut_key);
         if (keep) {
@@ -1794,7 +1809,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
       if (cut) {
         const float pcut = __fdiv_rn(exp_weight(__fsub_rn(value_of(cut_key), m)), zf);
         ordered_slice<T>(
-            row, s, sh, [&](float x, uint32_t) { return key_of(__fdiv_rn(x, tf)) == cut_key; },
+            row, s, sh, [&](float x, uint32_t) { return key_of(scaled(x)) == cut_key; },
             [&](float, uint32_t e, uint32_t rnk) {
               const bool keep = before + rnk < n_keep;
               if (keep) kc++;

@@ -381,3 +381,17 @@ def test_pass_path_ties_and_sparse_rows():
     for cpu in ("1", "8"):
         os.environ["PB_PASS_CPU"] = cpu
         compare(x, rec, probs=False, label=f"pass sparse-finite cpu={cpu}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_power_of_two_temperatures_cooperative_path(dtype):
+    """Temperature-only and top-p rows (the cooperative path) at power-of-two temperatures, where the
+    kernel scales by the exact reciprocal; includes rows whose scaled keys are subnormal."""
+    B, V = 12, 6001
+    x = workloads.head_boosted(B, V, seed=77, dtype=torch.float32)
+    x[8:10] *= 1e-37  # x / 4 and x / 2 land among the subnormals
+    x = x.to(dtype)
+    t = [0.25, 0.5, 1.0, 2.0, 4.0, 0.125, 1.0, 2.0, 4.0, 2.0, 0.5, 8.0]
+    p = [1.0, 0.9, 1.0, 0.95, 0.5, 1.0, 0.99, 1.0, 1.0, 0.9, 0.7, 0.8]
+    u = np.random.default_rng(5).random(B)
+    compare(x, oracle.make_params(t, p, [0] * B, u), label=f"pow2 T {dtype}")
