@@ -221,15 +221,30 @@ __device__ Slice make_slice(const T* row, int64_t V, int rank, int C) {
   return s;
 }
 
-// Visit every element of the slice (any order per thread; no warp-collective work in f).
+// Visit every element of the slice (any order per thread; no warp-collective work in f). The
+// passes that call this re-read the slice from L2 and do tens of instructions per element, so each
+// thread keeps the loads of its next SLICE_AHEAD vectors in flight while it works on one.
+constexpr int SLICE_AHEAD = 3;
 template <typename T, typename F>
 __device__ __forceinline__ void for_slice(const T* row, const Slice& s, F&& f) {
   constexpr int EPV = Elem<T>::EPV;
   for (int64_t e = threadIdx.x; e < s.head_n; e += NT) f(Elem<T>::ld(row + e), (uint32_t)e);
   const uint4* vp = reinterpret_cast<const uint4*>(row + s.vec_e0);
+  const uint4 none = make_uint4(0u, 0u, 0u, 0u);
+  uint4 ahead[SLICE_AHEAD];
+#pragma unroll
+  for (int i = 0; i < SLICE_AHEAD; ++i) {
+    const int64_t v = threadIdx.x + (int64_t)i * NT;
+    ahead[i] = (v < s.nvec) ? __ldg(vp + v) : none;
+  }
   for (int64_t v = threadIdx.x; v < s.nvec; v += NT) {
+    const uint4 cur = ahead[0];
+#pragma unroll
+    for (int i = 0; i + 1 < SLICE_AHEAD; ++i) ahead[i] = ahead[i + 1];
+    const int64_t vn = v + (int64_t)SLICE_AHEAD * NT;
+    ahead[SLICE_AHEAD - 1] = (vn < s.nvec) ? __ldg(vp + vn) : none;
     float x[EPV];
-    Elem<T>::unpack(__ldg(vp + v), x);
+    Elem<T>::unpack(cur, x);
     const uint32_t e0 = (uint32_t)(s.vec_e0 + v * EPV);
 #pragma unroll
     for (int j = 0; j < EPV; ++j) f(x[j], e0 + j);
