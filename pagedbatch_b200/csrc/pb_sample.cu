@@ -473,22 +473,33 @@ __device__ int first_of_key(const uint64_t* a, int n, uint32_t key) {
 // inclusive scan, top-p cut and the draw. n <= 64; lanes 0..31 of one warp call.
 __device__ void warp_finish(uint64_t* K, int n, float m, bool topp, float pf, uint64_t u53, Finish* f) {
   const int lane = threadIdx.x & 31;
-  for (int i = n + lane; i < 64; i += 32) K[i] = 0ull;
-  __syncwarp();
+  // bitonic sort of the (up to) 64 composites, descending, in registers: lane l holds positions
+  // 2l (a) and 2l + 1 (b); padding (0) sorts last
+  uint64_t a = (2 * lane < n) ? K[2 * lane] : 0ull;
+  uint64_t b = (2 * lane + 1 < n) ? K[2 * lane + 1] : 0ull;
+#pragma unroll
   for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) {
-      const int lo = 2 * lane - (lane & (j - 1));
-      const int hi = lo + j;
-      const uint64_t x = K[lo], y = K[hi];
-      const bool desc = (lo & k) == 0;
-      if (desc ? (x < y) : (x > y)) {
-        K[lo] = y;
-        K[hi] = x;
+      const bool desc = ((2 * lane) & k) == 0;  // the same for both positions of a lane (k >= 2)
+      if (j == 1) {
+        if (desc ? (a < b) : (a > b)) {
+          const uint64_t t = a;
+          a = b;
+          b = t;
+        }
+      } else {
+        const bool lower = ((2 * lane) & j) == 0;  // partner positions differ by j: lanes by j / 2
+        const uint64_t oa = __shfl_xor_sync(0xFFFFFFFFu, a, j >> 1);
+        const uint64_t ob = __shfl_xor_sync(0xFFFFFFFFu, b, j >> 1);
+        a = (lower == desc) ? max(a, oa) : min(a, oa);
+        b = (lower == desc) ? max(b, ob) : min(b, ob);
       }
-      __syncwarp();
     }
   }
-  const uint64_t a = K[2 * lane], b = K[2 * lane + 1];
+  K[2 * lane] = a;
+  K[2 * lane + 1] = b;
+  __syncwarp();
   const uint64_t qa = (2 * lane < n) ? weight_q(value_of(comp_key(a)), m) : 0ull;
   const uint64_t qb = (2 * lane + 1 < n) ? weight_q(value_of(comp_key(b)), m) : 0ull;
   const uint64_t s = qa + qb;
