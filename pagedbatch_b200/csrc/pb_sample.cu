@@ -2611,7 +2611,8 @@ int launch(const Args& a, int C, cudaStream_t stream) {
   return PB_OK;
 }
 
-// Cluster size: enough CTAs to give every SM one, but slices of at least 16 KB.
+// Cluster size: enough CTAs to give every SM one, but slices of at least one staged chunk (a
+// slice shorter than a chunk pays the per-CTA start and finish for less than one ring stage).
 int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
   const char* env = getenv("PB_CLUSTER");
   if (env) {
@@ -2630,7 +2631,7 @@ int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
   const int64_t want = sms[dev];
   const int64_t bytes = vocab * es;
   int C = 1;
-  while (C < 8 && n_rows * C < want && bytes / (2 * C) >= 16384) C <<= 1;
+  while (C < 8 && n_rows * C < want && bytes / (2 * C) >= CHUNK_BYTES) C <<= 1;
   return C;
 }
 
