@@ -1,7 +1,10 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference implementation.
 
-Run in a container that has the reference checkout (default ``/root/reference``; override with
-``PAGEDBATCH_REF``):  ``python tests/golden/make_golden.py``. Writes ``tests/golden/golden.npz``.
+Run where the reference package can be imported: set ``PAGEDBATCH_REF`` to a checkout of
+pagedbatch (the directory holding ``pagedbatch/``), or install it into ``baseline/_ref``. Then
+``python tests/golden/make_golden.py [small|big|all]`` writes ``tests/golden/golden.npz`` (small rows
+and config 0) and/or ``tests/golden/golden_big.npz`` (the benchmark configurations at full
+vocabulary: config 2, config 2-flat, config 1, and top_p values that round to 1.0 in fp32).
 
 For every case row it records what the reference itself produces:
 
@@ -16,8 +19,9 @@ For every case row it records what the reference itself produces:
 * ``tie_cut``     — the top-p cut falls inside a group of equal keys, where the reference's unstable
                     sort picks arbitrary members (only the count is determined).
 
-Small rows are stored verbatim; the config-0 rows are stored as their generator seed plus a
-checksum of the regenerated logits.
+Small rows are stored verbatim; the benchmark rows are stored as their generator seed plus a
+checksum of the regenerated logits. For rows whose kept set is large, the probabilities are
+stored at a subset of the kept positions (the 64 largest and a seeded sample of the rest).
 """
 
 from __future__ import annotations
@@ -32,7 +36,17 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
-sys.path.insert(0, os.environ.get("PAGEDBATCH_REF", "/root/reference"))
+
+
+def _reference_path() -> str:
+    """Where the reference package is imported from: $PAGEDBATCH_REF, else baseline/_ref."""
+    for cand in (os.environ.get("PAGEDBATCH_REF"), os.path.join(REPO, "baseline", "_ref")):
+        if cand and os.path.isdir(os.path.join(cand, "pagedbatch")):
+            return cand
+    raise SystemExit("set PAGEDBATCH_REF to a pagedbatch checkout (the directory holding pagedbatch/)")
+
+
+sys.path.insert(0, _reference_path())
 
 from pagedbatch.config import SamplingParams as RefParams  # noqa: E402  (the reference)
 from pagedbatch.sampling import sample_token as ref_sample_token  # noqa: E402
@@ -132,23 +146,112 @@ def pack_cases(rows, cases, prefix):
     return out
 
 
-def main():
+def _digest(x: torch.Tensor) -> np.ndarray:
+    """sha256 of a CPU tensor's raw bytes (bf16 / fp16 as their 16-bit patterns)."""
+    t = x.contiguous()
+    raw = t.view(torch.int16).numpy() if t.dtype in (torch.bfloat16, torch.float16) else t.numpy()
+    return np.frombuffer(hashlib.sha256(raw.tobytes()).digest(), np.uint8)
+
+
+PROB_ALL = 512  # kept sets up to this size store every probability; larger ones a subset
+PROB_TOP = 64
+
+
+def pack_big(logits: torch.Tensor, cases, prefix: str, seed: int = 99):
+    """Cases over rows of a regenerated workload: kept sets in full (bit-packed), probabilities at
+    every kept position of small kept sets and at the PROB_TOP largest plus a seeded sample of the
+    other kept positions of large ones."""
+    rng = np.random.default_rng(seed)
+    V = logits.shape[1]
+    n = len(cases)
+    cols = {c: np.zeros(n, dt) for c, dt in [("row", np.int32), ("temp", np.float64), ("topk", np.int32),
+                                             ("topp", np.float64), ("seed", np.int64), ("ref_token", np.int64),
+                                             ("port_token", np.int64), ("margin", np.float64),
+                                             ("tie_cut", bool), ("kept_n", np.int64)]}
+    kept = np.zeros((n, V), bool)
+    pidx, pval, poff = [], [], [0]
+    for i, (rid, t, k, p, seed_i) in enumerate(cases):
+        row = logits[rid]
+        ref = ref_sample_token(row, RefParams(temperature=t, top_k=k, top_p=p), torch.Generator().manual_seed(seed_i))
+        port = torch_port.sample_row(row, t, k, p, torch.Generator().manual_seed(seed_i))
+        assert ref == port, f"torch port disagrees with the reference on {prefix} case {i}"
+        kp, pr, mg, tc = masked_info(row, t, k, p)
+        kept[i] = kp
+        pos = np.flatnonzero(kp)
+        if pos.size > PROB_ALL:
+            top = pos[np.argsort(-pr[pos], kind="stable")[:PROB_TOP]]
+            rest = np.setdiff1d(pos, top)
+            pos = np.sort(np.concatenate([top, rng.choice(rest, PROB_ALL - PROB_TOP, replace=False)]))
+        pidx.append(pos.astype(np.int32))
+        pval.append(pr[pos].astype(np.float32))
+        poff.append(poff[-1] + pos.size)
+        for c, v in [("row", rid), ("temp", t), ("topk", k), ("topp", p), ("seed", seed_i), ("ref_token", ref),
+                     ("port_token", port), ("margin", mg), ("tie_cut", tc), ("kept_n", int(kp.sum()))]:
+            cols[c][i] = v
+    out = {f"{prefix}_kept": np.packbits(kept, axis=1), f"{prefix}_probs_idx": np.concatenate(pidx),
+           f"{prefix}_probs": np.concatenate(pval), f"{prefix}_probs_off": np.array(poff, np.int64)}
+    out.update({f"{prefix}_{c}": v for c, v in cols.items()})
+    return out
+
+
+# top_p values just below 1.0 in float64: the first three round to 1.0 in fp32 (the reference
+# still takes its top-p branch, sampling.py:18, since the Python compare is in float64), the last
+# is the largest fp32 below 1.0
+P_NEAR_ONE = (1.0 - 2.0**-30, 1.0 - 2.0**-25, 0.99999999, 1.0 - 2.0**-24)
+
+
+def big_fixtures() -> dict:
     out = {}
-    rows, cases = small_cases()
-    out.update(pack_cases(rows, cases, "small"))
-    w = workloads.config0(seed=0)
-    out["cfg0_sha256"] = np.frombuffer(hashlib.sha256(w.logits.numpy().tobytes()).digest(), np.uint8)
-    cfg_rows = [w.logits[r] for r in range(w.rows)]
-    cfg_cases = [(r, sp.temperature, sp.top_k, sp.top_p, w.seeds[r]) for r, sp in enumerate(w.params)]
-    cfg_cases += [(r, 0.0, 0, 1.0, 0) for r in range(w.rows)]
-    packed = pack_cases(cfg_rows, cfg_cases, "cfg0")
-    del packed["cfg0_logits"]  # regenerated from the seed by the tests
-    out.update(packed)
-    path = os.path.join(HERE, "golden.npz")
-    np.savez_compressed(path, **out)
-    print(f"wrote {path}: {len(cases)} small cases over {len(rows)} rows, {len(cfg_cases)} config-0 cases, "
-          f"{os.path.getsize(path)/1e6:.2f} MB")
+    w2 = workloads.config2(seed=0)
+    out["cfg2_sha256"] = _digest(w2.logits)
+    cases = [(r, w2.params[r].temperature, w2.params[r].top_k, w2.params[r].top_p, w2.seeds[r]) for r in range(32)]
+    out.update(pack_big(w2.logits, cases, "cfg2"))
+    del w2
+    wf = workloads.config2_flat(seed=0)
+    out["cfg2flat_sha256"] = _digest(wf.logits)
+    cases = [(r, wf.params[r].temperature, wf.params[r].top_k, wf.params[r].top_p, wf.seeds[r]) for r in range(16)]
+    out.update(pack_big(wf.logits, cases, "cfg2flat"))
+    del wf
+    w1 = workloads.config1(seed=0)
+    out["cfg1_sha256"] = _digest(w1.logits)
+    cases = [(r, sp.temperature, sp.top_k, sp.top_p, w1.seeds[r]) for r, sp in enumerate(w1.params)]
+    out.update(pack_big(w1.logits, cases, "cfg1"))
+    del w1
+    w0 = workloads.config0(seed=0)
+    cases = []
+    for j, p in enumerate(P_NEAR_ONE):
+        for r in range(w0.rows):
+            t, k = ((1.0, 0), (0.8, 50), (1.0, 0), (1.3, 1000))[(j + r) % 4]
+            cases.append((r, t, k, p, 1000 + 8 * j + r))
+    out["p1_sha256"] = _digest(w0.logits)
+    out.update(pack_big(w0.logits, cases, "p1"))
+    return out
+
+
+def main(which: str = "all"):
+    if which in ("small", "all"):
+        out = {}
+        rows, cases = small_cases()
+        out.update(pack_cases(rows, cases, "small"))
+        w = workloads.config0(seed=0)
+        out["cfg0_sha256"] = np.frombuffer(hashlib.sha256(w.logits.numpy().tobytes()).digest(), np.uint8)
+        cfg_rows = [w.logits[r] for r in range(w.rows)]
+        cfg_cases = [(r, sp.temperature, sp.top_k, sp.top_p, w.seeds[r]) for r, sp in enumerate(w.params)]
+        cfg_cases += [(r, 0.0, 0, 1.0, 0) for r in range(w.rows)]
+        packed = pack_cases(cfg_rows, cfg_cases, "cfg0")
+        del packed["cfg0_logits"]  # regenerated from the seed by the tests
+        out.update(packed)
+        path = os.path.join(HERE, "golden.npz")
+        np.savez_compressed(path, **out)
+        print(f"wrote {path}: {len(cases)} small cases over {len(rows)} rows, {len(cfg_cases)} config-0 cases, "
+              f"{os.path.getsize(path)/1e6:.2f} MB")
+    if which in ("big", "all"):
+        out = big_fixtures()
+        path = os.path.join(HERE, "golden_big.npz")
+        np.savez_compressed(path, **out)
+        n = {g: len(out[f"{g}_temp"]) for g in ("cfg2", "cfg2flat", "cfg1", "p1")}
+        print(f"wrote {path}: {n}, {os.path.getsize(path)/1e6:.2f} MB")
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1] if len(sys.argv) > 1 else "all")
