@@ -72,6 +72,7 @@ extern "C" {
 #define PB_PATH_GREEDY 1
 #define PB_PATH_SMALL 2      /* top-k candidates resolved in shared memory */
 #define PB_PATH_LARGE 4      /* cluster-cooperative histogram selection over the row */
+#define PB_PATH_STREAM 8     /* settled by the persistent streaming kernel (with GREEDY or SMALL) */
 
 /* One row's sampling parameters (SamplingParams, config.py:134-158, plus the row's draw). */
 typedef struct pb_row_params {

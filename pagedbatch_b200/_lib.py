@@ -22,7 +22,7 @@ ERRORS = {-1: "invalid argument", -2: "vocabulary too large", -3: "kernel launch
 ROW_OK, ROW_NONFINITE, ROW_BAD_UNIFORM, ROW_TIMEOUT, ROW_INTERNAL, ROW_BAD_PARAMS = 0, 1, 2, 4, 8, 16
 ROW_FALLBACK = 32
 CAND_FALLBACK, CAND_GREEDY, CAND_MAX_CAP = 0x100, 0x200, 2048
-PATH_GREEDY, PATH_SMALL, PATH_LARGE = 1, 2, 4
+PATH_GREEDY, PATH_SMALL, PATH_LARGE, PATH_STREAM = 1, 2, 4, 8
 MAX_VOCAB = 1 << 24
 
 # struct pb_row_params / pb_row_info (include/pagedbatch_b200.h)

@@ -13,7 +13,9 @@ from dataclasses import dataclass
 
 @dataclass
 class SamplingParams:
-    """Per-request decoding parameters (a subset of the OpenAI API surface)."""
+    """What one request asks of the sampler and the decode loop: how many tokens, the sampling
+    knobs (temperature 0 means greedy; top_k 0 and top_p 1 switch those filters off), whether to
+    ignore the end-of-sequence token, a seed for the request's own generator, and extra stop ids."""
 
     max_tokens: int = 64
     temperature: float = 1.0

@@ -158,6 +158,20 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Stores to shared memory under a predicate, without a branch (a predicated-off store costs an
+// issue slot and nothing else).
+__device__ __forceinline__ void st_shared_v4_if(bool p, void* dst, uint4 v) {
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.u32 q, %0, 0;\n @q st.shared.v4.u32 [%1], {%2, %3, %4, %5};\n}\n" ::"r"((uint32_t)p),
+      "r"(smem_addr(dst)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+      : "memory");
+}
+__device__ __forceinline__ void st_shared_u32_if(bool p, void* dst, uint32_t v) {
+  asm volatile("{\n .reg .pred q;\n setp.ne.u32 q, %0, 0;\n @q st.shared.u32 [%1], %2;\n}\n" ::"r"((uint32_t)p),
+               "r"(smem_addr(dst)), "r"(v)
+               : "memory");
+}
+
 // ---- warp / block scans -------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
@@ -183,25 +197,53 @@ __device__ __forceinline__ T warp_sum(T v) {
   return v;
 }
 
+// Barrier of a thread group: B = 0 is the whole CTA (__syncthreads); B = 1 is named barrier 1
+// over the first 256 threads (warps 0-7), the consumer warps of the streaming kernel, whose other
+// warps run their own loops and never reach it.
+template <int B>
+__device__ __forceinline__ void bsync() {
+  if constexpr (B == 0) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+  }
+}
+
+// Barrier of the group that also returns whether any of its threads passed v != 0.
+template <int B>
+__device__ __forceinline__ bool bsync_or(bool v) {
+  if constexpr (B == 0) {
+    return __syncthreads_or(v) != 0;
+  } else {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+  }
+}
+
 // Block-wide exclusive scan of one value per thread; `scratch` holds >= nwarps + 1 entries.
-// Returns the exclusive prefix; *total receives the block total. Contains __syncthreads().
-template <typename T, int NT>
+// Returns the exclusive prefix; *total receives the block total. Contains barriers of group B.
+template <typename T, int NT, int B = 0>
 __device__ __forceinline__ T block_excl_scan(T v, T* scratch, T* total) {
   constexpr int NW = NT / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   T inc = warp_incl_scan(v);
   if (lane == 31) scratch[warp] = inc;
-  __syncthreads();
+  bsync<B>();
   if (warp == 0) {
     T s = (lane < NW) ? scratch[lane] : T(0);
     T si = warp_incl_scan(s);
     if (lane < NW) scratch[lane] = si - s;
     if (lane == NW - 1) scratch[NW] = si;
   }
-  __syncthreads();
+  bsync<B>();
   T r = scratch[warp] + inc - v;
   *total = scratch[NW];
-  __syncthreads();
+  bsync<B>();
   return r;
 }
 

@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -71,6 +72,7 @@ struct Args {
   pb_row_info* out_info;
   float* out_probs;
   const pb_row_info* only_fallback;  // if set: sample only the rows whose status there is PB_ROW_FALLBACK
+  int32_t complement;    // skip the rows the streaming kernel settled (it ran first on the stream)
   uint8_t* cand_out;     // vocabulary-parallel shard mode: per-row candidate records (else null)
   int32_t cand_cap;      // entries per record
   int64_t vocab_offset;  // global index of this shard's first column
@@ -155,7 +157,21 @@ struct Elem;
 template <>
 struct Elem<float> {
   static constexpr int ES = 4, EPV = 4;
+  static constexpr uint32_t NEG_INF_WORD = 0xFF800000u;  // a 32-bit word of -inf elements
   __device__ static float ld(const float* p) { return __ldg(p); }
+  // NaN-propagating max of the elements of two words, lane by lane (a word holds 1 or 2 elements)
+  __device__ static uint32_t max2(uint32_t a, uint32_t b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(__uint_as_float(a)), "f"(__uint_as_float(b)));
+    return __float_as_uint(r);
+  }
+  // the largest element of a word, as fp32 (NaN if it holds one)
+  __device__ static float word_max(uint32_t w) { return __uint_as_float(w); }
+  // element q (runtime index < EPV) of a vector, as fp32
+  __device__ static float elem(uint4 v, int q) {
+    const uint32_t w = (q & 2) ? ((q & 1) ? v.w : v.z) : ((q & 1) ? v.y : v.x);
+    return __uint_as_float(w);
+  }
   __device__ static void unpack(uint4 v, float* x) {
     x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y);
     x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
@@ -164,8 +180,23 @@ struct Elem<float> {
 template <>
 struct Elem<__nv_bfloat16> {
   static constexpr int ES = 2, EPV = 8;
+  static constexpr uint32_t NEG_INF_WORD = 0xFF80FF80u;
   __device__ static float ld(const __nv_bfloat16* p) {
     return __uint_as_float(((uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p))) << 16);
+  }
+  __device__ static uint32_t max2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  __device__ static float word_max(uint32_t w) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(__uint_as_float(w << 16)), "f"(__uint_as_float(w & 0xFFFF0000u)));
+    return r;
+  }
+  __device__ static float elem(uint4 v, int q) {
+    const uint32_t w = (q & 4) ? ((q & 2) ? v.w : v.z) : ((q & 2) ? v.y : v.x);
+    return __uint_as_float((q & 1) ? (w & 0xFFFF0000u) : (w << 16));
   }
   __device__ static void unpack(uint4 v, float* x) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -179,7 +210,25 @@ struct Elem<__nv_bfloat16> {
 template <>
 struct Elem<__half> {
   static constexpr int ES = 2, EPV = 8;
+  static constexpr uint32_t NEG_INF_WORD = 0xFC00FC00u;
   __device__ static float ld(const __half* p) { return __half2float(__ldg(p)); }
+  __device__ static uint32_t max2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  __device__ static float word_max(uint32_t w) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;"
+        : "=f"(r)
+        : "f"(__half2float(__ushort_as_half((unsigned short)(w & 0xFFFF)))),
+          "f"(__half2float(__ushort_as_half((unsigned short)(w >> 16)))));
+    return r;
+  }
+  __device__ static float elem(uint4 v, int q) {
+    const uint32_t w = (q & 4) ? ((q & 2) ? v.w : v.z) : ((q & 2) ? v.y : v.x);
+    return __half2float(__ushort_as_half((unsigned short)((q & 1) ? (w >> 16) : (w & 0xFFFF))));
+  }
   __device__ static void unpack(uint4 v, float* x) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -319,7 +368,8 @@ __device__ __forceinline__ void warp_append(bool pass, uint32_t key, uint32_t id
 }
 
 // Block-wide (sum, min, max) of one value per thread; every thread gets all three. All threads
-// call; the caller separates two calls (and any later use of sh.red) with a barrier.
+// of barrier group B call; the caller separates two calls (and any later use of sh.red) with a barrier.
+template <int B = 0>
 __device__ __forceinline__ void block_sum_min_max(uint32_t v, uint32_t mn, uint32_t mx, Shared& sh, uint32_t* sum_out,
                                                   uint32_t* min_out, uint32_t* max_out) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -331,7 +381,7 @@ __device__ __forceinline__ void block_sum_min_max(uint32_t v, uint32_t mn, uint3
     sh.red[NW + w] = mx;
     sh.red[4 * NW + w] = mn;
   }
-  __syncthreads();
+  bsync<B>();
   uint32_t s = 0, lo = 0xFFFFFFFFu, hi = 0;
 #pragma unroll
   for (int i = 0; i < NW; ++i) {
@@ -349,9 +399,9 @@ __device__ __forceinline__ void block_sum_min_max(uint32_t v, uint32_t mn, uint3
 // held keys below lo (fillers) never count. The bisection stops once at most BUCKET keys lie in
 // [lo, hi). exact = false returns lo (a lower bound: at least k keys are >= lo, and at most BUCKET
 // more than are >= the k-th); exact = true finishes inside the bucket and returns the k-th key
-// itself. Every thread returns the same key. All threads call; the caller puts a barrier between
-// this and the next use of sh.red.
-template <int N>
+// itself. Every thread returns the same key. All threads of barrier group B call; the caller puts a
+// barrier between this and the next use of sh.red.
+template <int N, int B = 0>
 __device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint32_t lo, uint32_t c_lo,
                                      uint64_t hi_excl, bool exact, Shared& sh) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -365,7 +415,7 @@ __device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint3
     for (int j = 0; j < N; ++j) c += (key[j] >= mid) ? 1u : 0u;
     c = __reduce_add_sync(0xFFFFFFFFu, c);
     if (lane == 0) sh.red[2 * NW + par * NW + w] = c;
-    __syncthreads();
+    bsync<B>();
     uint32_t tot = 0;
 #pragma unroll
     for (int i = 0; i < NW; ++i) tot += sh.red[2 * NW + par * NW + i];
@@ -381,7 +431,7 @@ __device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint3
   if (!exact || hi - lo <= 1) return lo;
   // c_lo - c_hi <= BUCKET keys lie in [lo, hi); the answer is the (k - c_hi)-th largest of them
   if (threadIdx.x == 0) sh.bucket_n = 0;
-  __syncthreads();
+  bsync<B>();
 #pragma unroll
   for (int j = 0; j < N; ++j) {
     if (key[j] >= lo && (uint64_t)key[j] < hi) {
@@ -389,7 +439,7 @@ __device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint3
       if (pos < BUCKET) sh.bucket[pos] = key[j];
     }
   }
-  __syncthreads();
+  bsync<B>();
   if (w == 0) {
     const uint32_t n = min(sh.bucket_n, BUCKET);
     const uint32_t mine = (uint32_t)lane < n ? sh.bucket[lane] : 0u;
@@ -403,7 +453,7 @@ __device__ uint32_t block_kth_select(const uint32_t (&key)[N], uint32_t k, uint3
     const uint32_t hit = __ballot_sync(0xFFFFFFFFu, (uint32_t)lane < n && gt < r && r <= ge);
     if (hit && lane == __ffs(hit) - 1) sh.bucket_kth = mine;  // lanes that hit hold equal keys
   }
-  __syncthreads();
+  bsync<B>();
   return sh.bucket_kth;
 }
 
@@ -670,12 +720,13 @@ __device__ void reduce_and_find(cg::cluster_group& cluster, int C, uint64_t* hq,
 // Lower bound of the k-th largest key the CTA holds when every thread offers one key it holds (0:
 // none): each warp sorts its 32 offers (bitonic, in registers), takes its ceil(k / NW)-th largest,
 // and the CTA takes the smallest of those, so the NW warps hold at least k keys at or above it.
-// k <= OFFER_KMAX. Every thread returns the same key. All threads call; the caller separates two
-// calls (and any other use of sh.red[3 * NW ...]) with a barrier.
+// k <= OFFER_KMAX. Every thread returns the same key. All threads of barrier group B call; the
+// caller separates two calls (and any other use of sh.red[3 * NW ...]) with a barrier.
 constexpr int OFFER_KMAX = 32 * NW;
 // k up to which thresholds come from the offer bound (above it the bound, the smallest of a few
 // offers per warp, is too loose to thin candidates out; an exact bisection takes those)
 constexpr int OFFER_PREFER = 16 * NW;
+template <int B = 0>
 __device__ uint32_t block_offer_bound(uint32_t key, int k, Shared& sh) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -690,7 +741,7 @@ __device__ uint32_t block_offer_bound(uint32_t key, int k, Shared& sh) {
   }
   const uint32_t kj = __shfl_sync(0xFFFFFFFFu, key, (k + NW - 1) / NW - 1);
   if (lane == 0) sh.red[3 * NW + w] = kj;
-  __syncthreads();
+  bsync<B>();
   uint32_t mn = 0xFFFFFFFFu;
 #pragma unroll
   for (int i = 0; i < NW; ++i) mn = min(mn, sh.red[3 * NW + i]);
@@ -725,8 +776,9 @@ __device__ __forceinline__ int dense_slots(uint32_t n) {
 
 // Raise the candidate threshold sh.thr_f to the tie floor of a lower bound of the kth_rank-th
 // largest candidate held in the per-thread slots (slot j of thread t at candB[j * NT + t]) and
-// drop the candidates below it. Returns this thread's new slot count. All threads call; a barrier
-// separates two calls. Kept out of line so the streaming loop stays small.
+// drop the candidates below it. Returns this thread's new slot count. All threads of barrier group
+// B call; a barrier separates two calls. Kept out of line so the streaming loop stays small.
+template <int B = 0>
 __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank, float tf, Shared& sh,
                                          uint32_t* count_out = nullptr) {
   const int tid = threadIdx.x;
@@ -736,11 +788,11 @@ __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank,
 #pragma unroll
     for (int j = 0; j < SLOTS; ++j)
       if (j < nc) top = max(top, comp_key(candB[j * NT + tid]));
-    const uint32_t lo = block_offer_bound(top, kth_rank, sh);
+    const uint32_t lo = block_offer_bound<B>(top, kth_rank, sh);
     const float old = sh.thr_f;
-    __syncthreads();  // every thread has read the old threshold and sh.red
+    bsync<B>();  // every thread has read the old threshold and sh.red
     if (tid == 0 && lo > KEY_NEG_INF) sh.thr_f = fmaxf(old, tie_floor(value_of(lo), tf));
-    __syncthreads();
+    bsync<B>();
     const uint32_t fk = key_of(sh.thr_f);
     int w = 0;
 #pragma unroll
@@ -764,13 +816,14 @@ __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank,
     mx = max(mx, kk[j]);
   }
   uint32_t tot, kmin, kmax;
-  block_sum_min_max((uint32_t)nc, mn, mx, sh, &tot, &kmin, &kmax);
+  block_sum_min_max<B>((uint32_t)nc, mn, mx, sh, &tot, &kmin, &kmax);
   if ((int)tot < kth_rank) return nc;  // fewer candidates than k: nothing to raise
   // a lower bound of the kth_rank-th candidate (at most BUCKET more candidates above it)
-  const uint32_t kth_raw = block_kth_select<SLOTS>(kk, (uint32_t)kth_rank, kmin, tot, (uint64_t)kmax + 1, false, sh);
-  __syncthreads();  // every thread has read the old threshold
+  const uint32_t kth_raw =
+      block_kth_select<SLOTS, B>(kk, (uint32_t)kth_rank, kmin, tot, (uint64_t)kmax + 1, false, sh);
+  bsync<B>();  // every thread has read the old threshold
   if (tid == 0) sh.thr_f = tie_floor(value_of(kth_raw), tf);
-  __syncthreads();
+  bsync<B>();
   const uint32_t fk = key_of(sh.thr_f);
   // A large k keeps about k candidates, and a thread may hold many of them: deal the kept ones out
   // evenly (entry i of the dense list goes to slot i / NT of thread i % NT), so that no thread
@@ -783,13 +836,13 @@ __device__ __noinline__ int compact_slots(uint64_t* candB, int nc, int kth_rank,
     keep += (j < nc && kk[j] >= fk) ? 1u : 0u;
   }
   uint32_t kept;
-  uint32_t pos = block_excl_scan<uint32_t, NT>(keep, sh.s32, &kept);  // every slot is read first
+  uint32_t pos = block_excl_scan<uint32_t, NT, B>(keep, sh.s32, &kept);  // every slot is read first
 #pragma unroll
   for (int j = 0; j < SLOTS; ++j) {
     if (j < nc && kk[j] >= fk) candB[pos++] = v[j];
   }
   if (count_out && tid == 0) *count_out = kept;
-  __syncthreads();
+  bsync<B>();
   return (kept > (uint32_t)tid) ? (int)((kept - (uint32_t)tid + NT - 1) / NT) : 0;
 }
 
@@ -916,6 +969,8 @@ __device__ void finish_survivors(uint64_t* K, int nk, float m, bool topp_active,
   __syncthreads();
 }
 
+#include "pb_stream.cuh"
+
 template <typename T>
 __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
@@ -947,6 +1002,14 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
   const int64_t V = a.vocab;
   // rows another launch already settled: every CTA of the cluster leaves before any cluster step
   if (a.only_fallback && a.only_fallback[item].status != PB_ROW_FALLBACK) return;
+  if (a.complement && fast_mode(a.params[item], V) != F_NONE) {
+    // the streaming kernel took this row; it left a mark if it could not settle it
+    griddep_wait();
+    const bool retry = a.cand_out ? reinterpret_cast<const pb_cand_header*>(a.cand_out + item * record_bytes(a.cand_cap))
+                                            ->flags == F_CAND_RETRY
+                                  : a.out_token[item] == F_RETRY;
+    if (!retry) return;
+  }
 
   if (tid == 0) {
     const pb_row_params p = a.params[item];
@@ -2583,30 +2646,81 @@ __global__ void __launch_bounds__(NT, 2) pass_kernel(PassArgs a) {
   }
 }
 
-template <typename T>
-int launch(const Args& a, int C, cudaStream_t stream) {
-  // the dynamic shared memory limit is a per-device function attribute
-  static unsigned long long configured = 0;  // bit d: device d configured
+// Per-device one-time set-up (a function attribute, a device property): a bit per device, set
+// atomically, so that concurrent first calls from several host threads are safe (the set-up itself
+// is idempotent).
+struct DeviceOnce {
+  std::atomic<unsigned long long> done{0};
+  bool test(int dev) const { return (done.load(std::memory_order_acquire) >> dev) & 1ull; }
+  void set(int dev) { done.fetch_or(1ull << dev, std::memory_order_acq_rel); }
+};
+
+int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= 64) return PB_E_DEVICE;
+  return PB_OK;
+}
+
+// Per-device cached integer (0 = not yet known).
+struct DeviceInt {
+  std::atomic<int> v[64] = {};
+};
+
+int sm_count() {
+  static DeviceInt cache;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
-  if (!(configured & (1ull << dev))) {
+  if (current_device(&dev) != PB_OK) dev = 0;
+  int n = cache.v[dev].load(std::memory_order_relaxed);
+  if (!n) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache.v[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+template <typename T>
+int launch(const Args& a, int C, cudaStream_t stream, bool pdl = false) {
+  // the dynamic shared memory limit is a per-device function attribute
+  static DeviceOnce configured;
+  int dev = 0;
+  if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
+  if (!configured.test(dev)) {
     if (cudaFuncSetAttribute(sample_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM) != cudaSuccess)
       return PB_E_DEVICE;
-    configured |= 1ull << dev;
+    configured.set(dev);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.n_rows * C), 1, 1);
   cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = DYN_SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // after the streaming kernel: launch early, the CTAs that need its results wait for it
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, sample_kernel<T>, a) != cudaSuccess) return PB_E_LAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  return PB_OK;
+}
+
+// The persistent streaming kernel: one CTA per SM (at most one per row).
+template <typename T>
+int launch_stream(const FastArgs& a, cudaStream_t stream) {
+  static DeviceOnce configured;
+  int dev = 0;
+  if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
+  if (!configured.test(dev)) {
+    if (cudaFuncSetAttribute(stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM) != cudaSuccess)
+      return PB_E_DEVICE;
+    configured.set(dev);
+  }
+  const int64_t grid = std::min<int64_t>(a.n_rows, sm_count());
+  stream_kernel<T><<<(unsigned)grid, F_THREADS, F_SMEM, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
   return PB_OK;
 }
@@ -2619,32 +2733,22 @@ int cluster_size_for(int64_t n_rows, int64_t vocab, int es) {
     const int c = atoi(env);
     if (c == 1 || c == 2 || c == 4 || c == 8) return c;
   }
-  static int sms[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!sms[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    sms[dev] = n;
-  }
-  const int64_t want = sms[dev];
+  const int64_t want = sm_count();
   const int64_t bytes = vocab * es;
   int C = 1;
   while (C < 8 && n_rows * C < want && bytes / (2 * C) >= CHUNK_BYTES) C <<= 1;
   return C;
 }
 
-
 int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,
                  int64_t* out_token, pb_row_info* out_info, cudaStream_t stream) {
-  static unsigned long long configured = 0;  // bit d: device d configured
+  static DeviceOnce configured;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
-  if (!(configured & (1ull << dev))) {
+  if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
+  if (!configured.test(dev)) {
     if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_SMEM) != cudaSuccess)
       return PB_E_DEVICE;
-    configured |= 1ull << dev;
+    configured.set(dev);
   }
   MergeArgs m;
   m.records = records;
@@ -2659,29 +2763,16 @@ int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32
   return PB_OK;
 }
 
-int sm_count() {
-  static int sms[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!sms[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    sms[dev] = n;
-  }
-  return sms[dev];
-}
-
 constexpr int PASS_SMEM = RING_BYTES + SLOTS * NT * 8;
 
 // Resident pass CTAs per SM (the grid is one wave of them); 1 when the query fails.
 int pass_ctas_per_sm(int es) {
-  static int occ[64][2] = {};
+  static DeviceInt occ[2];
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
+  if (current_device(&dev) != PB_OK) dev = 0;
   const int which = (es == 4) ? 0 : 1;
-  if (!occ[dev][which]) {
+  int have = occ[which].v[dev].load(std::memory_order_relaxed);
+  if (!have) {
     int n = 0;
     cudaError_t rc;
     if (es == 4) {
@@ -2692,9 +2783,10 @@ int pass_ctas_per_sm(int es) {
       cudaFuncSetAttribute(pass_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
       rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pass_kernel<__nv_bfloat16>, NT, PASS_SMEM);
     }
-    occ[dev][which] = (rc == cudaSuccess && n > 0) ? n : 1;
+    have = (rc == cudaSuccess && n > 0) ? n : 1;
+    occ[which].v[dev].store(have, std::memory_order_relaxed);
   }
-  return occ[dev][which];
+  return have;
 }
 
 // Geometry of a pass launch: staged chunks per unit, units per row, total units, grid.
@@ -2746,14 +2838,14 @@ int64_t ws_bytes_for(int64_t n_rows, const PassPlan& pl) {
 
 template <typename T>
 int launch_pass(const PassArgs& a, int grid, cudaStream_t stream) {
-  static unsigned long long configured = 0;  // bit d: device d configured
+  static DeviceOnce configured;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
+  if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
   const int smem = PASS_SMEM;
-  if (!(configured & (1ull << dev))) {
+  if (!configured.test(dev)) {
     if (cudaFuncSetAttribute(pass_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return PB_E_DEVICE;
-    configured |= 1ull << dev;
+    configured.set(dev);
   }
   pass_kernel<T><<<(unsigned)grid, NT, smem, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
@@ -2798,6 +2890,7 @@ int run_pass(const void* logits, int dtype, int es, int64_t n_rows, int64_t voca
   a.out_info = out_info;
   a.out_probs = nullptr;
   a.only_fallback = info;
+  a.complement = 0;
   a.cand_out = nullptr;
   a.cand_cap = 0;
   a.vocab_offset = 0;
@@ -2817,17 +2910,75 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES
 
 // Device address of g_noalloc_scratch on the current device, looked up once per device (in host
 // code the array's name is only a host-side stand-in, never a device address).
+// The cached address stays valid for the process's primary context on that device; a caller that
+// resets the device (cudaDeviceReset) must not use this entry point again in the same process.
 int noalloc_scratch(uint8_t** out) {
-  static uint8_t* addr[64] = {};
+  static std::atomic<uint8_t*> addr[64] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PB_E_DEVICE;
-  if (!addr[dev]) {
+  if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
+  uint8_t* a = addr[dev].load(std::memory_order_acquire);
+  if (!a) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return PB_E_DEVICE;
-    addr[dev] = static_cast<uint8_t*>(p);
+    a = static_cast<uint8_t*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  *out = addr[dev];
+  *out = a;
   return PB_OK;
+}
+// Which kernels pb_sample / pb_candidates run. The persistent streaming kernel (greedy rows and
+// top_k <= F_KMAX, then the cluster kernel on the same stream over every other row and the rows it
+// marked) pays off when each SM has several rows to pipeline: measured on a B200, [1024, 128256]
+// bf16 rows take 99 us instead of 193 us, while [256, 128256] fp32 (1.7 rows per SM) is faster on
+// the cluster kernel alone (41 us against 46 us). PB_PATH=cluster / PB_PATH=stream force one.
+bool stream_path_enabled(int64_t n_rows) {
+  const char* env = getenv("PB_PATH");
+  if (env && strcmp(env, "cluster") == 0) return false;
+  if (env && strcmp(env, "stream") == 0) return true;
+  return n_rows >= 3 * (int64_t)sm_count();
+}
+
+// Consumer waits of the streaming kernel: WAIT_POLLS polls, or PB_TEST_STAGE_POLLS (a test of the
+// bounded-wait path sets 0, so that every wait on a staged chunk gives up at once).
+int stage_poll_limit() {
+  const char* env = getenv("PB_TEST_STAGE_POLLS");
+  if (env) {
+    const int v = atoi(env);
+    if (v >= 0 && v <= WAIT_POLLS) return v;
+  }
+  return WAIT_POLLS;
+}
+
+template <typename T>
+int run_rows(Args a, int es, cudaStream_t st) {
+  const int C = cluster_size_for(a.n_rows, a.vocab, es);
+  if (a.out_probs || !stream_path_enabled(a.n_rows)) {
+    a.complement = 0;
+    return launch<T>(a, C, st);
+  }
+  FastArgs f;
+  f.logits = a.logits;
+  f.n_rows = a.n_rows;
+  f.vocab = a.vocab;
+  f.row_stride = a.row_stride;
+  f.row_index = a.row_index;
+  f.params = a.params;
+  f.out_token = a.out_token;
+  f.out_info = a.out_info;
+  f.cand_out = a.cand_out;
+  f.cand_cap = a.cand_cap;
+  f.vocab_offset = a.vocab_offset;
+  f.poll_limit = stage_poll_limit();
+  int rc = launch_stream<T>(f, st);
+  if (rc != PB_OK) return rc;
+  a.complement = 1;
+  return launch<T>(a, C, st, getenv("PB_NO_PDL") == nullptr);
+}
+
+int run_rows_dtype(const Args& a, int dtype, int es, cudaStream_t st) {
+  if (dtype == PB_DTYPE_F32) return run_rows<float>(a, es, st);
+  if (dtype == PB_DTYPE_BF16) return run_rows<__nv_bfloat16>(a, es, st);
+  return run_rows<__half>(a, es, st);
 }
 }  // namespace
 
@@ -2855,14 +3006,11 @@ int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int6
   a.out_info = out_info;
   a.out_probs = out_probs;
   a.only_fallback = nullptr;
+  a.complement = 0;
   a.cand_out = nullptr;
   a.cand_cap = 0;
   a.vocab_offset = 0;
-  const int C = cluster_size_for(n_rows, vocab, es);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
-  if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
-  return launch<__half>(a, C, st);
+  return run_rows_dtype(a, dtype, es, static_cast<cudaStream_t>(stream));
 }
 
 int64_t pb_record_bytes(int32_t cap) { return record_bytes(cap); }
@@ -2891,14 +3039,11 @@ int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t shard_v
   a.out_info = nullptr;
   a.out_probs = nullptr;
   a.only_fallback = nullptr;
+  a.complement = 0;
   a.cand_out = static_cast<uint8_t*>(out_records);
   a.cand_cap = cap;
   a.vocab_offset = vocab_offset;
-  const int C = cluster_size_for(n_rows, shard_vocab, es);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
-  if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
-  return launch<__half>(a, C, st);
+  return run_rows_dtype(a, dtype, es, static_cast<cudaStream_t>(stream));
 }
 
 int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,

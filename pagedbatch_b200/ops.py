@@ -30,7 +30,9 @@ def pack_params(temperature, top_p, top_k, uniform) -> np.ndarray:
     rec = np.zeros(n, dtype=_lib.ROW_PARAMS)
     rec["temperature"] = temperature
     rec["top_p"] = top_p
-    rec["top_k"] = top_k
+    # any top_k at or above the vocabulary switches the filter off (sampling.py:15), so values past
+    # the int32 field saturate instead of failing
+    rec["top_k"] = np.minimum(np.asarray(top_k, dtype=np.int64), np.iinfo(np.int32).max)
     rec["uniform"] = uniform
     return rec
 

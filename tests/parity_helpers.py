@@ -1,0 +1,62 @@
+"""Shared GPU-parity helpers: run a batch through the C ABI and compare with the CPU oracle."""
+
+import os
+
+import numpy as np
+import torch
+
+import oracle
+from pagedbatch_b200 import ops
+
+INFO_FIELDS = ("thr_key", "n_tie_kept", "kept_count", "status", "z_q", "kept_q")
+
+
+def run_gpu(logits_dev, rec, row_index=None, probs=True):
+    params = ops.params_tensor(rec, logits_dev.device)
+    ri = None if row_index is None else torch.as_tensor(np.asarray(row_index, np.int32), device=logits_dev.device)
+    tok, info, pr = ops.sample(logits_dev, params, ri, with_info=True, with_probs=probs)
+    torch.cuda.synchronize()
+    return tok.cpu().numpy(), ops.info_records(info), (pr.cpu().numpy() if probs else None)
+
+
+def _check(g_tok, g_info, o_tok, o_info, label):
+    bad = np.flatnonzero(g_tok != o_tok)
+    assert bad.size == 0, f"{label}: tokens differ at rows {bad[:10]}: gpu {g_tok[bad[:10]]} oracle {o_tok[bad[:10]]}"
+    for f in INFO_FIELDS:
+        d = np.flatnonzero(g_info[f] != o_info[f])
+        assert d.size == 0, f"{label}: info.{f} differs at rows {d[:10]}: gpu {g_info[f][d[:10]]} oracle {o_info[f][d[:10]]}"
+    assert np.array_equal(g_info["max_key"], o_info["max_key"], equal_nan=True), label
+
+
+def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""):
+    """GPU against the oracle. With probs, the launch that writes probabilities (the cluster kernel
+    alone) is checked, and then the same rows without probabilities through the streaming kernel
+    (then the cluster kernel on the rows it leaves)."""
+    dev = logits_cpu.to(device)
+    g_tok, g_info, g_pr = run_gpu(dev, rec, row_index, probs)
+    o_tok, o_info, o_pr = oracle.sample(logits_cpu, rec, row_index, want_probs=probs)
+    _check(g_tok, g_info, o_tok, o_info, label)
+    if probs:
+        ok = g_info["status"] == 0
+        same = g_pr[ok].view(np.uint32) == o_pr[ok].view(np.uint32)
+        rows_bad = np.flatnonzero(~same.all(axis=1))
+        assert rows_bad.size == 0, f"{label}: probs differ on rows {rows_bad[:10]}"
+        # and the streaming kernel first (the default for batches with several rows per SM)
+        forced = "PB_PATH" not in os.environ
+        if forced:
+            os.environ["PB_PATH"] = "stream"
+        try:
+            s_tok, s_info, _ = run_gpu(dev, rec, row_index, False)
+        finally:
+            if forced:
+                os.environ.pop("PB_PATH", None)
+        _check(s_tok, s_info, o_tok, o_info, label + " (streaming kernel)")
+    return g_tok, g_info
+
+
+def rec_for(params, uniforms):
+    return oracle.make_params(
+        [p.temperature for p in params], [p.top_p for p in params], [p.top_k for p in params], uniforms
+    )
+
+

@@ -61,3 +61,10 @@ def test_no_cpu_fallback():
 def test_row_selection_validation():
     with pytest.raises(ValueError, match="rows="):
         sample_tokens(torch.zeros(3, 4, device="meta"), [SamplingParams()] * 2, [torch.Generator()] * 2)
+
+
+def test_huge_top_k_saturates():
+    """The reference accepts any top_k >= 0 and treats top_k >= vocab as no filter (sampling.py:15):
+    a top_k past int32 must pack (saturated), not raise."""
+    rec = pack_rows([SamplingParams(temperature=1.0, top_k=2**40)], np.array([0.5]))
+    assert rec["top_k"][0] == 2**31 - 1

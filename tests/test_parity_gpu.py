@@ -15,42 +15,9 @@ import torch
 
 import oracle
 from pagedbatch_b200 import _lib, ops, workloads
+from parity_helpers import INFO_FIELDS, _check, compare, rec_for, run_gpu  # noqa: F401
 
 pytestmark = pytest.mark.gpu
-
-INFO_FIELDS = ("thr_key", "n_tie_kept", "kept_count", "status", "z_q", "kept_q")
-
-
-def run_gpu(logits_dev, rec, row_index=None, probs=True):
-    params = ops.params_tensor(rec, logits_dev.device)
-    ri = None if row_index is None else torch.as_tensor(np.asarray(row_index, np.int32), device=logits_dev.device)
-    tok, info, pr = ops.sample(logits_dev, params, ri, with_info=True, with_probs=probs)
-    torch.cuda.synchronize()
-    return tok.cpu().numpy(), ops.info_records(info), (pr.cpu().numpy() if probs else None)
-
-
-def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""):
-    dev = logits_cpu.to(device)
-    g_tok, g_info, g_pr = run_gpu(dev, rec, row_index, probs)
-    o_tok, o_info, o_pr = oracle.sample(logits_cpu, rec, row_index, want_probs=probs)
-    bad = np.flatnonzero(g_tok != o_tok)
-    assert bad.size == 0, f"{label}: tokens differ at rows {bad[:10]}: gpu {g_tok[bad[:10]]} oracle {o_tok[bad[:10]]}"
-    for f in INFO_FIELDS:
-        d = np.flatnonzero(g_info[f] != o_info[f])
-        assert d.size == 0, f"{label}: info.{f} differs at rows {d[:10]}: gpu {g_info[f][d[:10]]} oracle {o_info[f][d[:10]]}"
-    assert np.array_equal(g_info["max_key"], o_info["max_key"], equal_nan=True), label
-    if probs:
-        ok = g_info["status"] == 0
-        same = g_pr[ok].view(np.uint32) == o_pr[ok].view(np.uint32)
-        rows_bad = np.flatnonzero(~same.all(axis=1))
-        assert rows_bad.size == 0, f"{label}: probs differ on rows {rows_bad[:10]}"
-    return g_tok, g_info
-
-
-def rec_for(params, uniforms):
-    return oracle.make_params(
-        [p.temperature for p in params], [p.top_p for p in params], [p.top_k for p in params], uniforms
-    )
 
 
 @pytest.fixture(autouse=True)
