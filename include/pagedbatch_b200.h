@@ -96,7 +96,8 @@ typedef struct pb_row_info {
 } pb_row_info;
 
 /*
- * Sample one token for each of n_rows rows, in one launch on `stream`.
+ * Sample one token for each of n_rows rows, in one or two launches on `stream` (see
+ * pb_sample_launches).
  *
  * Replaces: pagedbatch/sampling.py:10-27 sample_token, called per row at pagedbatch/engine.py:139.
  *
@@ -190,6 +191,14 @@ PB_API int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t 
  */
 PB_API int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,
                     int64_t* out_token, pb_row_info* out_info, void* stream);
+
+/*
+ * Kernel launches pb_sample / pb_candidates make for a batch of this shape on the current device:
+ * 1 (the cluster kernel alone) or 2 (the persistent streaming kernel over the greedy and
+ * top_k <= 128 rows, then the cluster kernel over the others and the rows it could not settle).
+ * No counterpart in the reference; a diagnostic for benchmarks and tests. -1 on bad arguments.
+ */
+PB_API int pb_sample_launches(int64_t n_rows, int64_t vocab, int dtype, int with_probs);
 
 /* Order-preserving 32-bit key of a float (NaN above +inf, -0 == +0); host helper for tests. */
 PB_API uint32_t pb_key_of(float x);

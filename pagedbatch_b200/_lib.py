@@ -59,6 +59,7 @@ EXPORTS = (
     "pb_candidates",
     "pb_merge",
     "pb_record_bytes",
+    "pb_sample_launches",
     "pb_key_of",
     "pb_exp",
     "pb_strerror",
@@ -102,6 +103,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     L.pb_candidates.restype = i32
     L.pb_merge.argtypes = [vp, i32, i64, i32, vp, vp, vp, vp]
     L.pb_merge.restype = i32
+    L.pb_sample_launches.argtypes = [i64, i64, i32, i32]
+    L.pb_sample_launches.restype = i32
     L.pb_record_bytes.argtypes = [i32]
     L.pb_record_bytes.restype = i64
     L.pb_key_of.argtypes = [ctypes.c_float]

@@ -197,15 +197,17 @@ __device__ __forceinline__ T warp_sum(T v) {
   return v;
 }
 
-// Barrier of a thread group: B = 0 is the whole CTA (__syncthreads); B = 1 is named barrier 1
-// over the first 256 threads (warps 0-7), the consumer warps of the streaming kernel, whose other
-// warps run their own loops and never reach it.
+// Barrier of a thread group: B = 0 is the whole CTA (__syncthreads); B = 1 and B = 2 are named
+// barrier 1 over the first 256 or 512 threads (warps 0-7 or 0-15): a group of warps (the consumer
+// warps of the streaming kernel) whose CTA's other warps run their own loops and never reach it.
 template <int B>
 __device__ __forceinline__ void bsync() {
   if constexpr (B == 0) {
     __syncthreads();
-  } else {
+  } else if constexpr (B == 1) {
     asm volatile("bar.sync 1, 256;" ::: "memory");
+  } else {
+    asm volatile("bar.sync 1, 512;" ::: "memory");
   }
 }
 
@@ -216,11 +218,19 @@ __device__ __forceinline__ bool bsync_or(bool v) {
     return __syncthreads_or(v) != 0;
   } else {
     uint32_t r;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}\n"
-        : "=r"(r)
-        : "r"((uint32_t)v)
-        : "memory");
+    if constexpr (B == 1) {
+      asm volatile(
+          "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+          : "=r"(r)
+          : "r"((uint32_t)v)
+          : "memory");
+    } else {
+      asm volatile(
+          "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 512, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+          : "=r"(r)
+          : "r"((uint32_t)v)
+          : "memory");
+    }
     return r != 0;
   }
 }

@@ -3015,6 +3015,13 @@ int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int6
 
 int64_t pb_record_bytes(int32_t cap) { return record_bytes(cap); }
 
+int pb_sample_launches(int64_t n_rows, int64_t vocab, int dtype, int with_probs) {
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
+  if (n_rows == 0) return 0;
+  return (!with_probs && stream_path_enabled(n_rows)) ? 2 : 1;
+}
+
 int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t row_stride,
                   const int32_t* row_index, const pb_row_params* params, int64_t vocab_offset, int32_t cap,
                   void* out_records, void* stream) {

@@ -14,7 +14,7 @@
 //     no multicast), waiting on each stage's "empty" mbarrier and arming its "full" one with the
 //     copy's byte count. It runs ahead across row boundaries, so the next row's first chunks are in
 //     flight while a row is closed.
-//   * warps 0..7: the consumers. Per chunk they wait on the stage's full barrier, copy their vectors
+//   * warps 0..15: the consumers. Per chunk they wait on the stage's full barrier, copy their vectors
 //     to registers, arrive on its empty barrier (nothing else), and track the row's max, its first
 //     maximum (greedy rows) and the candidates >= a running threshold (top-k rows) in per-thread
 //     slots; they meet (named barrier 1) only for the first threshold of a row and at checkpoints.
@@ -26,7 +26,8 @@
 // Every wait is bounded; a wait that gives up makes the whole CTA stop, let its issued copies land,
 // and report PB_ROW_TIMEOUT for its rows.
 
-constexpr int F_CW = NW;                    // consumer warps (the block helpers' group: 256 threads)
+constexpr int F_CW = 16;                    // consumer warps (barrier group 2: 512 threads)
+constexpr int F_CT = F_CW * 32;             // consumer threads
 constexpr int F_PROD = F_CW;                // producer warp
 constexpr int F_FIN = F_CW + 1;             // finisher warp
 constexpr int F_THREADS = (F_CW + 2) * 32;  // 320
@@ -36,8 +37,8 @@ constexpr int F_RING = F_NSTAGE * F_CHUNK;
 constexpr int F_LCAP = 512;                 // candidates one row hands to the finisher
 constexpr int F_KMAX = OFFER_PREFER;        // largest top_k settled here (thresholds from the offer bound)
 constexpr int F_SMAX = 256;                 // survivors the finisher orders
-constexpr int F_VSL = 16;                   // 16-byte vectors each consumer thread can hold as candidates
-constexpr int F_CAND = F_VSL * NT * 16 + F_VSL * NT * 4;  // the vectors and their first element's index
+constexpr int F_VSL = 8;                    // 16-byte vectors each consumer thread can hold as candidates
+constexpr int F_CAND = F_VSL * F_CT * 16 + F_VSL * F_CT * 4;  // the vectors and their first element's index
 constexpr int F_SMEM = F_RING + F_CAND + 2 * F_LCAP * 8;
 constexpr int64_t F_RETRY = -2;             // out_token mark: the cluster kernel samples this row
 constexpr int32_t F_CAND_RETRY = 0x400;     // the same mark in a shard record's flags
@@ -90,10 +91,13 @@ struct FastShared {
   int64_t issued[F_NSTAGE];                  // last chunk issued into each stage (-1: none)
   volatile int32_t abort;                    // a wait gave up: every role stops
   FastList lh[2];
-  float wbest[NW], wmx[NW];
-  uint32_t wbidx[NW];
-  uint32_t cpb[2][NW];  // per checkpoint (alternating): each warp's share of the offer bound
-  int32_t lfail;        // the wait for a free list buffer gave up (written before a barrier)
+  float wbest[F_CW], wmx[F_CW];
+  uint32_t wbidx[F_CW];
+  uint32_t cpb[2][F_CW];  // per checkpoint (alternating): each consumer warp's share of the offer bound
+  uint32_t ob[F_CW];      // each consumer warp's share of a row's first threshold
+  uint32_t s32[F_CW + 2]; // scan scratch of the consumer group
+  int32_t cp_flags[3];    // checkpoint flags (timeout 4, overflow 2), rotating so a reset never races a write
+  int32_t lfail;          // the wait for a free list buffer gave up (written before a barrier)
 };
 
 // Bounded wait that also gives up once another role has set `abort`.
@@ -443,6 +447,31 @@ __device__ void f_finisher(const FastArgs& a, FastShared& fs, uint64_t* lists) {
 
 // ---- consumers ------------------------------------------------------------------------------------
 
+// The offer bound of the consumer group: every thread offers one key (0: none); each warp sorts
+// its 32 offers (bitonic, in registers) and publishes its ceil(k / F_CW)-th largest; the smallest
+// over the warps is reached by at least k offers. Every thread returns the same key. One barrier;
+// `slot` must not be read by another call until a later barrier.
+__device__ __forceinline__ uint32_t f_offer_bound(uint32_t key, int k, uint32_t* slot, FastShared& fs) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, key, stride);
+      const bool desc = (lane & size) == 0, lower = (lane & stride) == 0;
+      key = (lower == desc) ? max(key, o) : min(key, o);
+    }
+  }
+  const uint32_t kj = __shfl_sync(0xFFFFFFFFu, key, (k + F_CW - 1) / F_CW - 1);
+  if (lane == 0) slot[warp] = kj;
+  bsync<2>();
+  uint32_t mn = 0xFFFFFFFFu;
+#pragma unroll
+  for (int w = 0; w < F_CW; ++w) mn = min(mn, slot[w]);
+  return mn;
+}
+
+
 // Candidates of a top-k row are whole 16-byte vectors: a thread keeps (in shared memory) every
 // vector of its own that holds a value at or above the threshold, with the index of its first
 // element. Storing a vector costs no per-element work in the streaming loop; the values are
@@ -462,28 +491,34 @@ __device__ __forceinline__ float vec_max(uint4 v) {
   return E::word_max(E::max2(E::max2(v.x, v.y), E::max2(v.z, v.w)));
 }
 
+// w[j] for a runtime j (an unrolled select: the array stays in registers)
+template <int N>
+__device__ __forceinline__ uint4 reg_pick(const uint4 (&w)[N], int j) {
+  uint4 v = w[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i)
+    if (i == j) v = w[i];
+  return v;
+}
+
 template <typename T>
-__device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const uint4* ring, uint4* cand,
+__device__ void f_consumers(const FastArgs& a, FastShared& fs, const uint4* ring, uint4* cand,
                             uint64_t* lists) {
   using E = Elem<T>;
   constexpr int EPV = E::EPV;
   constexpr int CV = F_CHUNK / 16;  // vectors per chunk
-  constexpr int VPT = CV / NT;          // vectors per thread per chunk
+  constexpr int VPT = CV / F_CT;          // vectors per thread per chunk
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t V = a.vocab;
-  uint4* vs = cand;                                                // held vectors: slot j of thread t at j * NT + t
-  uint32_t* vb = reinterpret_cast<uint32_t*>(cand + F_VSL * NT);  // index of each held vector's first element
+  uint4* vs = cand;                                                // held vectors: slot j of thread t at j * F_CT + t
+  uint32_t* vb = reinterpret_cast<uint32_t*>(cand + F_VSL * F_CT);  // index of each held vector's first element
   uint32_t seq = 0, lseq = 0;
   int cp = 0;              // checkpoints passed (their flag words rotate over three slots)
   bool timed_out = false;  // this warp gave up waiting on a staged chunk (warp-uniform)
   bool stop = false;       // the CTA gave up (uniform over the consumers)
-  if (tid == 0) {
-    for (int i = 0; i < 3; ++i) {
-      sh.cp_flags[i] = 0;
-      sh.cp_count[i] = 0;
-    }
-  }
-  bsync<1>();
+  if (tid == 0)
+    for (int i = 0; i < 3; ++i) fs.cp_flags[i] = 0;
+  bsync<2>();
   for (int64_t item = blockIdx.x; item < a.n_rows && !stop; item += gridDim.x) {
     const pb_row_params p = a.params[item];
     const int mode = fast_mode(p, V);
@@ -511,12 +546,14 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
       uint4 w[VPT];
       if (nv == CV && !timed_out) {
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) w[j] = buf[j * NT + tid];
+        for (int j = 0; j < VPT; ++j) w[j] = buf[j * F_CT + tid];
       } else {
         const uint4 pad = make_uint4(E::NEG_INF_WORD, E::NEG_INF_WORD, E::NEG_INF_WORD, E::NEG_INF_WORD);
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) w[j] = (j * NT + tid < nv && !timed_out) ? buf[j * NT + tid] : pad;
+        for (int j = 0; j < VPT; ++j) w[j] = (j * F_CT + tid < nv && !timed_out) ? buf[j * F_CT + tid] : pad;
       }
+      __syncwarp();
+      if (lane == 0 && !timed_out) mbar_arrive(&fs.empty[st]);  // the vectors are in registers
       // per-vector and per-chunk maxima on the packed words (NaN-propagating)
       uint32_t vm2[VPT];
 #pragma unroll
@@ -533,12 +570,12 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
           for (int j = 0; j < VPT; ++j) hit |= (E::word_max(vm2[j]) == tm) ? (1u << j) : 0u;
           const int j = __ffs(hit) - 1;
           float x[EPV];
-          E::unpack(buf[j * NT + tid], x);
+          E::unpack(reg_pick(w, j), x);
           int jj = EPV - 1;
 #pragma unroll
           for (int q = EPV - 1; q >= 0; --q)
             if (x[q] == tm) jj = q;
-          bidx = e_base + (uint32_t)((c * CV + j * NT) * EPV + jj);
+          bidx = e_base + (uint32_t)((c * CV + j * F_CT) * EPV + jj);
           bestv = tm;
         }
       } else {
@@ -546,20 +583,20 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
           // first threshold: a lower bound of the row's k-th value from this chunk (each warp's
           // ceil(k/8)-th largest per-thread maximum, the smallest over the warps), as a tie floor
           uint32_t lo = 0;
-          if (nv * EPV >= k) lo = block_offer_bound<1>(key_of(tm), k, sh);  // nv is the same for all
+          if (nv * EPV >= k) lo = f_offer_bound(key_of(tm), k, fs.ob, fs);  // nv is the same for all
           t = (lo > KEY_NEG_INF) ? tie_floor(value_of(lo), tf) : -INFINITY;  // (same in every thread)
         }
         if (!row_ovf && !timed_out && tm >= t) {
           // keep every vector that reaches t: predicated stores into the next free slots
           uint32_t hit = 0;  // (padding holds -inf: only real vectors)
 #pragma unroll
-          for (int j = 0; j < VPT; ++j) hit |= (E::word_max(vm2[j]) >= t && j * NT + tid < nv) ? (1u << j) : 0u;
+          for (int j = 0; j < VPT; ++j) hit |= (E::word_max(vm2[j]) >= t && j * F_CT + tid < nv) ? (1u << j) : 0u;
           while (hit) {  // usually one vector
             const int j = __ffs(hit) - 1;
             hit &= hit - 1;
             const int sl = min(nc, F_VSL - 1);  // (a store past the last slot only happens on overflow)
-            vs[sl * NT + tid] = buf[j * NT + tid];
-            vb[sl * NT + tid] = e_base + (uint32_t)((c * CV + j * NT) * EPV);
+            vs[sl * F_CT + tid] = reg_pick(w, j);
+            vb[sl * F_CT + tid] = e_base + (uint32_t)((c * CV + j * F_CT) * EPV);
             ++nc;
           }
           if (nc > F_VSL) {
@@ -568,15 +605,13 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
           }
         }
       }
-      __syncwarp();
-      if (lane == 0 && !timed_out) mbar_arrive(&fs.empty[st]);
       if (!greedy && f_checkpoint(c, nch)) {
         // checkpoint (one barrier): agree on timeouts and overflow, and raise the threshold by the
         // offer bound of the values held (every thread offers its largest; each warp's
         // ceil(k/8)-th largest offer, the smallest over the warps, is reached by at least k of
         // them), then each thread drops its vectors below the new threshold
         float top = -INFINITY;
-        for (int j = 0; j < nc; ++j) top = fmax_nan(top, vec_max<T>(vs[j * NT + tid]));
+        for (int j = 0; j < nc; ++j) top = fmax_nan(top, vec_max<T>(vs[j * F_CT + tid]));
         uint32_t key = nc > 0 ? key_of(top) : 0u;
 #pragma unroll
         for (int size = 2; size <= 32; size <<= 1) {
@@ -587,19 +622,19 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
             key = (lower == desc) ? max(key, o) : min(key, o);
           }
         }
-        const uint32_t kj = __shfl_sync(0xFFFFFFFFu, key, (k + NW - 1) / NW - 1);
+        const uint32_t kj = __shfl_sync(0xFFFFFFFFu, key, (k + F_CW - 1) / F_CW - 1);
         const bool wovf = __any_sync(0xFFFFFFFFu, ovf);
         if (lane == 0) {
           fs.cpb[cp & 1][warp] = kj;
           const int mine = ((timed_out || fs.abort) ? 4 : 0) | (wovf ? 2 : 0);
-          if (mine) atomicOr(&sh.cp_flags[cp % 3], mine);
+          if (mine) atomicOr(&fs.cp_flags[cp % 3], mine);
         }
-        bsync<1>();
-        const int f = sh.cp_flags[cp % 3];
+        bsync<2>();
+        const int f = fs.cp_flags[cp % 3];
         uint32_t lo = 0xFFFFFFFFu;
 #pragma unroll
-        for (int w2 = 0; w2 < NW; ++w2) lo = min(lo, fs.cpb[cp & 1][w2]);
-        if (tid == 0) sh.cp_flags[(cp + 2) % 3] = 0;
+        for (int w2 = 0; w2 < F_CW; ++w2) lo = min(lo, fs.cpb[cp & 1][w2]);
+        if (tid == 0) fs.cp_flags[(cp + 2) % 3] = 0;
         ++cp;
         if (f & 4) {
           stop = true;
@@ -610,11 +645,11 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
           t = fmaxf(t, tie_floor(value_of(lo), tf));  // (same in every thread)
           int kept = 0;
           for (int j = 0; j < nc; ++j) {
-            const uint4 v = vs[j * NT + tid];
+            const uint4 v = vs[j * F_CT + tid];
             if (vec_max<T>(v) >= t) {
               if (kept != j) {
-                vs[kept * NT + tid] = v;
-                vb[kept * NT + tid] = vb[j * NT + tid];
+                vs[kept * F_CT + tid] = v;
+                vb[kept * F_CT + tid] = vb[j * F_CT + tid];
               }
               ++kept;
             }
@@ -626,7 +661,7 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
     if (stop) break;
     // scalar head and tail: greedy rows compare them (first index wins among equal values); top-k
     // rows collect them below, as single elements
-    for (int64_t e = tid; e < r.head_n + r.tail_n; e += NT) {
+    for (int64_t e = tid; e < r.head_n + r.tail_n; e += F_CT) {
       const int64_t ei = (e < r.head_n) ? e : r.tail_e0 + (e - r.head_n);
       const float xv = E::ld(r.row + ei);
       runmax = fmax_nan(runmax, xv);
@@ -651,12 +686,12 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
         fs.wbest[warp] = bestv;
         fs.wbidx[warp] = bidx;
         fs.wmx[warp] = runmax;
-        if (timed_out || fs.abort) atomicOr(&sh.cp_flags[cp % 3], 4);
+        if (timed_out || fs.abort) atomicOr(&fs.cp_flags[cp % 3], 4);
       }
-      bsync<1>();
+      bsync<2>();
       {
-        const int f = sh.cp_flags[cp % 3];
-        if (tid == 0) sh.cp_flags[(cp + 2) % 3] = 0;
+        const int f = fs.cp_flags[cp % 3];
+        if (tid == 0) fs.cp_flags[(cp + 2) % 3] = 0;
         ++cp;
         if (f & 4) {
           stop = true;
@@ -664,7 +699,7 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
         }
       }
       if (tid == 0) {
-        for (int w = 1; w < NW; ++w) {
+        for (int w = 1; w < F_CW; ++w) {
           if (fs.wbest[w] > bestv || (fs.wbest[w] == bestv && fs.wbidx[w] < bidx)) {
             bestv = fs.wbest[w];
             bidx = fs.wbidx[w];
@@ -700,7 +735,7 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
           }
         }
       }
-      bsync<1>();  // fs.wbest / wbidx / wmx are read before the next row writes them
+      bsync<2>();  // fs.wbest / wbidx / wmx are read before the next row writes them
       continue;
     }
 
@@ -713,11 +748,11 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
     if (!row_ovf) {
       for (int j = 0; j < nc; ++j) {
         float x[EPV];
-        E::unpack(vs[j * NT + tid], x);
+        E::unpack(vs[j * F_CT + tid], x);
 #pragma unroll
         for (int q = 0; q < EPV; ++q) cnt += (x[q] >= t) ? 1u : 0u;
       }
-      for (int64_t e = tid; e < r.head_n + r.tail_n; e += NT) {
+      for (int64_t e = tid; e < r.head_n + r.tail_n; e += F_CT) {
         const int64_t ei = (e < r.head_n) ? e : r.tail_e0 + (e - r.head_n);
         cnt += (E::ld(r.row + ei) >= t) ? 1u : 0u;
       }
@@ -725,7 +760,7 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
     const int b = (int)(lseq & 1);
     if (tid == 0) fs.lfail = f_wait(&fs.lfree[b], ((lseq >> 1) & 1) ^ 1, WAIT_POLLS, &fs.abort) ? 0 : 1;
     uint32_t total;
-    uint32_t pos = block_excl_scan<uint32_t, NT, 1>(cnt, sh.s32, &total);  // (publishes fs.wmx, lfail)
+    uint32_t pos = block_excl_scan<uint32_t, F_CT, 2>(cnt, fs.s32, &total);  // (publishes fs.wmx, lfail)
     if (fs.lfail) {
       stop = true;
       if (tid == 0) fs.abort = 1;
@@ -733,7 +768,7 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
     }
     float mraw = fs.wmx[0];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) mraw = fmax_nan(mraw, fs.wmx[w]);
+    for (int w = 1; w < F_CW; ++w) mraw = fmax_nan(mraw, fs.wmx[w]);
     const float m = __fdiv_rn(mraw, tf);
     const uint32_t mk = key_of(m);
     const bool retry = row_ovf || total == 0 || total > (uint32_t)F_LCAP || mk >= KEY_POS_INF || mk <= KEY_NEG_INF;
@@ -741,19 +776,19 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, Shared& sh, const
       uint64_t* L = lists + b * F_LCAP;
       for (int j = 0; j < nc; ++j) {
         float x[EPV];
-        E::unpack(vs[j * NT + tid], x);
-        const uint32_t e0 = vb[j * NT + tid];
+        E::unpack(vs[j * F_CT + tid], x);
+        const uint32_t e0 = vb[j * F_CT + tid];
 #pragma unroll
         for (int q = 0; q < EPV; ++q)
           if (x[q] >= t) L[pos++] = compose(key_of(x[q]), e0 + (uint32_t)q);
       }
-      for (int64_t e = tid; e < r.head_n + r.tail_n; e += NT) {
+      for (int64_t e = tid; e < r.head_n + r.tail_n; e += F_CT) {
         const int64_t ei = (e < r.head_n) ? e : r.tail_e0 + (e - r.head_n);
         const float xv = E::ld(r.row + ei);
         if (xv >= t) L[pos++] = compose(key_of(xv), (uint32_t)ei);
       }
     }
-    bsync<1>();  // the list is written; every thread is done with fs.wmx and its vectors
+    bsync<2>();  // the list is written; every thread is done with fs.wmx and its vectors
     if (tid == 0) {
       FastList h;
       h.item = item;
@@ -776,7 +811,6 @@ template <typename T>
 __global__ void __launch_bounds__(F_THREADS, 1) stream_kernel(FastArgs a) {
   extern __shared__ __align__(128) unsigned char dyn[];
   __shared__ FastShared fs;
-  __shared__ Shared sh;
   uint4* ring = reinterpret_cast<uint4*>(dyn);
   uint4* cand = reinterpret_cast<uint4*>(dyn + F_RING);
   uint64_t* lists = reinterpret_cast<uint64_t*>(dyn + F_RING + F_CAND);
@@ -801,7 +835,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) stream_kernel(FastArgs a) {
   } else if (warp == F_FIN) {
     f_finisher<T>(a, fs, lists);
   } else {
-    f_consumers<T>(a, fs, sh, ring, cand, lists);
+    f_consumers<T>(a, fs, ring, cand, lists);
   }
   __syncthreads();
   if (fs.abort && tid == 0) {

@@ -75,3 +75,19 @@ def test_argument_errors(lib):
     assert lib.pb_sample(vp(buf), 0, 0, 8, 8, None, vp(p), vp(tok), None, None, None) == 0  # nothing to do
     assert lib.pb_strerror(-2).decode().startswith("vocabulary")
     assert lib.pb_version() >= 100
+
+
+def test_launch_plan(lib, monkeypatch):
+    """pb_sample_launches (host only): the streaming kernel joins in for batches with several rows
+    per SM, never when probabilities are asked for; PB_PATH forces either path."""
+    monkeypatch.delenv("PB_PATH", raising=False)
+    sms = 148  # without a GPU the library assumes a B200's 148 SMs
+    assert lib.pb_sample_launches(256, 128256, 0, 0) == 1
+    assert lib.pb_sample_launches(3 * sms, 128256, 1, 0) == 2
+    assert lib.pb_sample_launches(1024, 64128, 1, 1) == 1
+    assert lib.pb_sample_launches(8, 49152, 7, 0) == -1
+    assert lib.pb_sample_launches(0, 49152, 0, 0) == 0
+    monkeypatch.setenv("PB_PATH", "stream")
+    assert lib.pb_sample_launches(8, 49152, 0, 0) == 2
+    monkeypatch.setenv("PB_PATH", "cluster")
+    assert lib.pb_sample_launches(4096, 49152, 0, 0) == 1
