@@ -11,10 +11,11 @@ N > 1 the line also carries the vocabulary-parallel configuration (config 3: [10
 split by columns over the N ranks, one NCCL all-gather per step).
 
 * value: sampled rows/s over the whole job, inputs resident in HBM. K steps are captured in one
-  CUDA graph (with a timing event between steps) and the graph is replayed until at least 200 ms
-  of steps are timed; each replay is timed with CUDA events; value and ms_per_step come from the
-  median replay (max over ranks), timing_stats gives the per-launch median and p99. Each step
-  reads one of 4 rotating input copies (4 x 131 MB > 126 MB L2), so every step streams from HBM.
+  CUDA graph and the graph is replayed until at least 200 ms of steps are timed, each replay
+  between CUDA events; value and ms_per_step come from the median replay (max over ranks);
+  timing_stats adds the per-launch median and p99 (from a copy of the graph with an event between
+  launches). Each step reads one of 4 rotating input copies (4 x 131 MB > 126 MB L2), so every
+  step streams from HBM.
 * e2e: the same metric through the public API ``sample_tokens`` with the logits in pinned host
   memory: host->device copy of the logits and parameters, the launch, device->host tokens.
 * roofline: algorithmic bytes (B*V*elem read once) per step / median step time, against the
@@ -334,7 +335,18 @@ def measure_vocab_parallel(world, rank, local, dist, steps: int, warmup: int):
     fallback = int((ops.info_records(info)["status"] == _lib.ROW_FALLBACK).sum())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        for i in range(20):  # soak
+        # soak ~0.6 s (the same number of steps on every rank) so the clock samples mean something
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 0.3:
+            step(n)
+            n += 1
+            if n % 50 == 0:
+                torch.cuda.synchronize(dev)
+        cnt = torch.tensor([2 * n], device=dev, dtype=torch.int64)
+        if dist:
+            dist.all_reduce(cnt, op=dist.ReduceOp.MAX)
+        for i in range(int(cnt.item()) - n):
             step(i)
         if dist:
             dist.barrier()

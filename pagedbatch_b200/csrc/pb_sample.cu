@@ -2005,6 +2005,7 @@ struct MergeArgs {
   const pb_row_params* params;
   int64_t* out_token;
   pb_row_info* out_info;
+  int32_t complement;  // merge only the rows the one-warp merge marked (it ran first on the stream)
 };
 
 // One CTA per row: the row's token from the union of its shards' survivors, by the same steps and
@@ -2017,6 +2018,10 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
   uint64_t* K = reinterpret_cast<uint64_t*>(dyn + MERGE_CAP * 8);  // the row's survivors
   const int64_t item = blockIdx.x;
   const int tid = threadIdx.x;
+  if (a.complement) {
+    griddep_wait();
+    if (a.out_token[item] != F_RETRY) return;
+  }
   const int64_t rb = record_bytes(a.cap);
   auto header = [&](int r) {
     return reinterpret_cast<const pb_cand_header*>(a.records + ((int64_t)r * a.n_rows + item) * rb);
@@ -2138,6 +2143,162 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
       o->z_q = info.z_q;
       o->kept_q = info.kept_q;
     }
+  }
+}
+
+// The merge with one warp per row (8 rows per CTA), by the finisher's steps: the union of the
+// records, cut to the entries at or above the largest k-th key among the shards that hold at least
+// k entries (a lower bound of the row's k-th key: such a shard alone holds k values at or above
+// its own k-th), sorted in registers, then the k-th key, the survivors, the top-p cut and the draw.
+// A row whose cut union is longer than F_LCAP is marked F_RETRY for merge_kernel.
+constexpr int MW_ROWS = 8;
+constexpr int MW_SMEM = MW_ROWS * F_LCAP * 8;
+
+__global__ void __launch_bounds__(MW_ROWS * 32) merge_warp_kernel(MergeArgs m) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  griddep_launch_dependents();  // merge_kernel (the long rows) may launch; it waits for this grid
+  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const int64_t item = (int64_t)blockIdx.x * MW_ROWS + wi;
+  if (item >= m.n_rows) return;  // (the whole warp; this kernel has no block-wide step)
+  uint64_t* L = reinterpret_cast<uint64_t*>(dyn) + wi * F_LCAP;
+  const int64_t rb = record_bytes(m.cap);
+  auto hdr = [&](int r) {
+    return reinterpret_cast<const pb_cand_header*>(m.records + ((int64_t)r * m.n_rows + item) * rb);
+  };
+  auto ent = [&](int r) { return reinterpret_cast<const uint64_t*>(hdr(r) + 1); };
+  const pb_row_params p = m.params[item];
+  int32_t fl = 0, total = 0;
+  float gmax = -INFINITY, bmk = 0.0f;
+  uint64_t best = 0;
+  for (int r = lane; r < m.n_shards; r += 32) {
+    const pb_cand_header h = *hdr(r);
+    fl |= h.flags;
+    total += h.count;
+    gmax = fmax_nan(gmax, h.max_key);
+    if ((h.flags & PB_CAND_GREEDY) && h.count == 1) {
+      const uint64_t e = ent(r)[0];
+      if (e > best) {
+        best = e;
+        bmk = h.max_key;
+      }
+    }
+  }
+  fl = (int32_t)__reduce_or_sync(0xFFFFFFFFu, (uint32_t)fl);
+  total = (int32_t)__reduce_add_sync(0xFFFFFFFFu, (uint32_t)total);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    gmax = fmax_nan(gmax, __shfl_xor_sync(0xFFFFFFFFu, gmax, o));
+    const uint64_t b2 = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const float m2 = __shfl_xor_sync(0xFFFFFFFFu, bmk, o);
+    if (b2 > best) {
+      best = b2;
+      bmk = m2;
+    }
+  }
+  const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
+  const uint32_t mk = key_of(gmax);
+  int mode = 0, status = PB_ROW_OK;  // mode 0 status only, 1 greedy, 2 merge
+  if (fl & PB_ROW_TIMEOUT) status = PB_ROW_TIMEOUT;
+  else if (bad) status = PB_ROW_BAD_PARAMS;
+  else if (p.temperature == 0.0) mode = 1;
+  else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) status = PB_ROW_NONFINITE;
+  else if (!(p.uniform >= 0.0 && p.uniform < 1.0)) status = PB_ROW_BAD_UNIFORM;
+  else if ((fl & (PB_CAND_FALLBACK | 0xFF)) || total > MERGE_CAP || total == 0) status = PB_ROW_FALLBACK;
+  else mode = 2;
+  if (mode == 1 && (fl & ~PB_CAND_GREEDY)) {  // a shard could not publish its maximum
+    status = PB_ROW_FALLBACK;
+    mode = 0;
+  }
+  if (mode == 2) {
+    const int kq = (p.top_k > 0) ? min(p.top_k, total) : total;
+    uint32_t lb = 0;
+    for (int r = 0; r < m.n_shards; ++r) {
+      const int cnt = hdr(r)->count;
+      if (cnt >= kq) {
+        uint32_t mn = 0xFFFFFFFFu;
+        for (int i = lane; i < cnt; i += 32) mn = min(mn, comp_key(ent(r)[i]));
+        lb = max(lb, __reduce_min_sync(0xFFFFFFFFu, mn));
+      }
+    }
+    int n = 0;
+    for (int r = 0; r < m.n_shards; ++r) {
+      const int cnt = hdr(r)->count;
+      const uint64_t* e = ent(r);
+      for (int i0 = 0; i0 < cnt; i0 += 32) {
+        const int i = i0 + lane;
+        const uint64_t v = (i < cnt) ? e[i] : 0ull;
+        const bool keep = i < cnt && comp_key(v) >= lb;
+        const uint32_t bl = __ballot_sync(0xFFFFFFFFu, keep);
+        const int at = n + __popc(bl & lanemask_lt());
+        if (keep && at < F_LCAP) L[at] = v;
+        n += __popc(bl);
+      }
+    }
+    __syncwarp();
+    FastArgs fa = {};
+    fa.out_token = m.out_token;
+    fa.out_info = m.out_info;
+    if (n > F_SMAX && n <= F_LCAP) {
+      // cut to the survivors first: the exact kq-th key by bisection, keys at or above it
+      constexpr int R = F_LCAP / 32;
+      uint64_t c[R];
+      uint32_t lo = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const int i = j * 32 + lane;
+        c[j] = (i < n) ? L[i] : 0ull;
+        if (i < n) lo = min(lo, comp_key(c[j]));
+        mx = max(mx, comp_key(c[j]));
+      }
+      lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+      uint64_t hi = (uint64_t)__reduce_max_sync(0xFFFFFFFFu, mx) + 1;
+      const int kk = min(p.top_k, n);
+      while (hi - lo > 1) {
+        const uint32_t mid = (uint32_t)(lo + ((hi - lo) >> 1));
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int j = 0; j < R; ++j) cnt += (j * 32 + lane < n && comp_key(c[j]) >= mid) ? 1u : 0u;
+        if ((int)__reduce_add_sync(0xFFFFFFFFu, cnt) >= kk) lo = mid;
+        else hi = mid;
+      }
+      int w = 0;
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const bool keep = j * 32 + lane < n && comp_key(c[j]) >= lo;
+        const uint32_t bl = __ballot_sync(0xFFFFFFFFu, keep);
+        if (keep) L[w + __popc(bl & lanemask_lt())] = c[j];
+        w += __popc(bl);
+      }
+      __syncwarp();
+      n = w;
+    }
+    if (n > F_SMAX) {
+      if (lane == 0) m.out_token[item] = F_RETRY;  // merge_kernel takes this row
+    } else if (n <= 64) {
+      finish_list<2, true>(fa, p, item, L, n, gmax, PB_PATH_SMALL);
+    } else if (n <= 128) {
+      finish_list<4, true>(fa, p, item, L, n, gmax, PB_PATH_SMALL);
+    } else {
+      finish_list<8, true>(fa, p, item, L, n, gmax, PB_PATH_SMALL);
+    }
+    return;
+  }
+  if (lane == 0) {
+    int64_t token = -1;
+    pb_row_info info = {};
+    info.status = status;
+    if (mode == 1) {
+      info.max_key = bmk;
+      info.thr_key = key_of(bmk);
+      info.n_tie_kept = 1;
+      info.kept_count = 1;
+      info.flags = PB_PATH_GREEDY;
+      token = comp_idx(best);
+    } else if (status == PB_ROW_NONFINITE || status == PB_ROW_BAD_UNIFORM || status == PB_ROW_TIMEOUT) {
+      info.max_key = gmax;
+    }
+    m.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
+    if (m.out_info) m.out_info[item] = info;
   }
 }
 
@@ -2746,7 +2907,8 @@ int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32
   int dev = 0;
   if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
   if (!configured.test(dev)) {
-    if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(merge_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MW_SMEM) != cudaSuccess)
       return PB_E_DEVICE;
     configured.set(dev);
   }
@@ -2758,7 +2920,21 @@ int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32
   m.params = params;
   m.out_token = out_token;
   m.out_info = out_info;
-  merge_kernel<<<(unsigned)n_rows, NT, MERGE_SMEM, stream>>>(m);
+  m.complement = 0;
+  merge_warp_kernel<<<(unsigned)((n_rows + MW_ROWS - 1) / MW_ROWS), MW_ROWS * 32, MW_SMEM, stream>>>(m);
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  m.complement = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)n_rows, 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = MERGE_SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, merge_kernel, m) != cudaSuccess) return PB_E_LAUNCH;
   if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
   return PB_OK;
 }

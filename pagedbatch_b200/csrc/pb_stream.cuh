@@ -18,19 +18,21 @@
 //     to registers, arrive on its empty barrier (nothing else), and track the row's max, its first
 //     maximum (greedy rows) and the candidates >= a running threshold (top-k rows) in per-thread
 //     slots; they meet (named barrier 1) only for the first threshold of a row and at checkpoints.
-//     At the end of a top-k row they shrink the candidates and hand them to the finisher through one
-//     of two list buffers, then go straight on to the next row.
-//   * warp F_FIN: the finisher. For each handed-off row: the exact k-th key, the survivors, their
-//     order (key desc, index asc), fixed-point weights, the top-p cut and the inverse-CDF draw, all
-//     in one warp, while the consumers stream the next row.
+//     At the end of a top-k row they hand the candidates to a finisher through one of the list
+//     buffers, then go straight on to the next row.
+//   * warps F_FIN..: the finishers (rows alternate between them). For each handed-off row: the
+//     exact k-th key, the survivors, their order (key desc, index asc), fixed-point weights, the
+//     top-p cut and the inverse-CDF draw, all in one warp, while the consumers stream on.
 // Every wait is bounded; a wait that gives up makes the whole CTA stop, let its issued copies land,
 // and report PB_ROW_TIMEOUT for its rows.
 
 constexpr int F_CW = 16;                    // consumer warps (barrier group 2: 512 threads)
 constexpr int F_CT = F_CW * 32;             // consumer threads
 constexpr int F_PROD = F_CW;                // producer warp
-constexpr int F_FIN = F_CW + 1;             // finisher warp
-constexpr int F_THREADS = (F_CW + 2) * 32;  // 320
+constexpr int F_NF = 2;                     // finisher warps (rows alternate between them)
+constexpr int F_NB = 2 * F_NF;              // list buffers (two per finisher)
+constexpr int F_FIN = F_CW + 1;             // first finisher warp
+constexpr int F_THREADS = (F_CW + 1 + F_NF) * 32;
 constexpr int F_CHUNK = CHUNK_BYTES;        // bytes per staged chunk (32 KB)
 constexpr int F_NSTAGE = 4;                 // 128 KB of copies in flight per SM
 constexpr int F_RING = F_NSTAGE * F_CHUNK;
@@ -39,7 +41,7 @@ constexpr int F_KMAX = OFFER_PREFER;        // largest top_k settled here (thres
 constexpr int F_SMAX = 256;                 // survivors the finisher orders
 constexpr int F_VSL = 8;                    // 16-byte vectors each consumer thread can hold as candidates
 constexpr int F_CAND = F_VSL * F_CT * 16 + F_VSL * F_CT * 4;  // the vectors and their first element's index
-constexpr int F_SMEM = F_RING + F_CAND + 2 * F_LCAP * 8;
+constexpr int F_SMEM = F_RING + F_CAND + F_NB * F_LCAP * 8;
 constexpr int64_t F_RETRY = -2;             // out_token mark: the cluster kernel samples this row
 constexpr int32_t F_CAND_RETRY = 0x400;     // the same mark in a shard record's flags
 static_assert(F_SMEM <= 227 * 1024, "one CTA per SM");
@@ -87,10 +89,10 @@ struct FastList {
 
 struct FastShared {
   uint64_t full[F_NSTAGE], empty[F_NSTAGE];  // ring: copy landed / every consumer warp done with it
-  uint64_t lfull[2], lfree[2];               // list buffers: handed off / finisher done with it
+  uint64_t lfull[F_NB], lfree[F_NB];         // list buffers: handed off / finisher done with it
   int64_t issued[F_NSTAGE];                  // last chunk issued into each stage (-1: none)
   volatile int32_t abort;                    // a wait gave up: every role stops
-  FastList lh[2];
+  FastList lh[F_NB];
   float wbest[F_CW], wmx[F_CW];
   uint32_t wbidx[F_CW];
   uint32_t cpb[2][F_CW];  // per checkpoint (alternating): each consumer warp's share of the offer bound
@@ -291,13 +293,13 @@ __device__ void warp_finish_sorted(const uint64_t (&a)[NPL], int n, float m, boo
   }
 }
 
-// Settle a top-k row from n <= 32 * NPL candidates at L (composites of raw key and index, which
-// hold every survivor): scaled keys, one sort, the kq-th scaled key at position kq - 1 (x / T is
+// Settle a top-k row from n <= 32 * NPL candidates at L (composites of raw key and index, or of
+// the scaled key with SCALED, which hold every survivor): scaled keys, one sort, the kq-th scaled key at position kq - 1 (x / T is
 // monotone), the survivors (the prefix with key >= it, ties included), then the record (shard
 // mode) or the draw. All 32 lanes call.
-template <int NPL>
+template <int NPL, bool SCALED = false>
 __device__ void finish_list(const FastArgs& a, const pb_row_params& p, int64_t item, const uint64_t* L, int n,
-                            float m) {
+                            float m, int32_t flags = PB_PATH_SMALL | PB_PATH_STREAM) {
   const int lane = threadIdx.x & 31;
   const float tf = (float)p.temperature;
   uint64_t v[NPL];
@@ -307,7 +309,7 @@ __device__ void finish_list(const FastArgs& a, const pb_row_params& p, int64_t i
     uint64_t c = 0;
     if (pos < n) {
       const uint64_t raw = L[pos];
-      c = compose(key_of(__fdiv_rn(value_of(comp_key(raw)), tf)), comp_idx(raw));
+      c = SCALED ? raw : compose(key_of(__fdiv_rn(value_of(comp_key(raw)), tf)), comp_idx(raw));
     }
     v[r] = c;
   }
@@ -351,7 +353,7 @@ __device__ void finish_list(const FastArgs& a, const pb_row_params& p, int64_t i
       o->kept_count = f.last + 1;
       o->status = f.ok ? PB_ROW_OK : PB_ROW_INTERNAL;
       o->max_key = m;
-      o->flags = PB_PATH_SMALL | PB_PATH_STREAM;
+      o->flags = flags;
       o->z_q = f.zq;
       o->kept_q = f.kept;
     }
@@ -426,14 +428,16 @@ __device__ void f_finish_row(const FastArgs& a, const pb_row_params& p, const Fa
 }
 
 template <typename T>
-__device__ void f_finisher(const FastArgs& a, FastShared& fs, uint64_t* lists) {
+__device__ void f_finisher(const FastArgs& a, FastShared& fs, uint64_t* lists, int fin) {
   const int lane = threadIdx.x & 31;
-  uint32_t lseq = 0;
+  uint32_t lseq = 0;  // top-k rows of this CTA so far (this warp takes every F_NF-th)
   for (int64_t item = blockIdx.x; item < a.n_rows; item += gridDim.x) {
     const pb_row_params p = a.params[item];
     if (fast_mode(p, a.vocab) != F_FILTER) continue;
-    const int b = (int)(lseq & 1);
-    if (!__all_sync(0xFFFFFFFFu, f_wait(&fs.lfull[b], (lseq >> 1) & 1, WAIT_POLLS, &fs.abort))) {
+    const uint32_t mine = lseq++;
+    if ((int)(mine % F_NF) != fin) continue;
+    const int b = (int)(mine % F_NB);
+    if (!__all_sync(0xFFFFFFFFu, f_wait(&fs.lfull[b], (mine / F_NB) & 1, WAIT_POLLS, &fs.abort))) {
       if (lane == 0) fs.abort = 1;
       return;
     }
@@ -441,7 +445,6 @@ __device__ void f_finisher(const FastArgs& a, FastShared& fs, uint64_t* lists) {
     f_finish_row(a, p, h, lists + b * F_LCAP);
     __syncwarp();  // the list is read and rewritten before the consumers may refill it
     if (lane == 0) mbar_arrive(&fs.lfree[b]);
-    ++lseq;
   }
 }
 
@@ -757,8 +760,8 @@ __device__ void f_consumers(const FastArgs& a, FastShared& fs, const uint4* ring
         cnt += (E::ld(r.row + ei) >= t) ? 1u : 0u;
       }
     }
-    const int b = (int)(lseq & 1);
-    if (tid == 0) fs.lfail = f_wait(&fs.lfree[b], ((lseq >> 1) & 1) ^ 1, WAIT_POLLS, &fs.abort) ? 0 : 1;
+    const int b = (int)(lseq % F_NB);
+    if (tid == 0) fs.lfail = f_wait(&fs.lfree[b], ((lseq / F_NB) & 1) ^ 1, WAIT_POLLS, &fs.abort) ? 0 : 1;
     uint32_t total;
     uint32_t pos = block_excl_scan<uint32_t, F_CT, 2>(cnt, fs.s32, &total);  // (publishes fs.wmx, lfail)
     if (fs.lfail) {
@@ -822,7 +825,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) stream_kernel(FastArgs a) {
       mbar_init(&fs.empty[s], F_CW);
       fs.issued[s] = -1;
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < F_NB; ++b) {
       mbar_init(&fs.lfull[b], 1);
       mbar_init(&fs.lfree[b], 1);
     }
@@ -832,8 +835,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) stream_kernel(FastArgs a) {
   __syncthreads();
   if (warp == F_PROD) {
     if ((tid & 31) == 0) f_producer<T>(a, fs, ring);
-  } else if (warp == F_FIN) {
-    f_finisher<T>(a, fs, lists);
+  } else if (warp >= F_FIN) {
+    f_finisher<T>(a, fs, lists, warp - F_FIN);
   } else {
     f_consumers<T>(a, fs, ring, cand, lists);
   }

@@ -27,19 +27,24 @@ def main():
         w = workloads.config3(rows=256)
         w1 = workloads.config1(rows=64)
         cases = [(w.logits, w.params), (w1.logits, w1.params)]
-        for logits, params in cases:
-            V = logits.shape[1]
-            lo, hi = V * rank // world, V * (rank + 1) // world
-            x = logits.cuda()
-            local = x[:, lo:hi].contiguous()
-            gens = [torch.Generator().manual_seed(i) for i in range(len(params))]
-            got = sample_tokens_vocab_parallel(local, params, gens)
-            gens = [torch.Generator().manual_seed(i) for i in range(len(params))]
-            want = sample_tokens(x, params, gens)
-            if got != want:
-                bad = [i for i in range(len(got)) if got[i] != want[i]]
-                print(f"rank {rank}: {len(bad)} rows differ, first {bad[:5]}", flush=True)
-                ok = False
+        # both shard kernels: the default choice for these sizes, and the streaming kernel forced
+        for path in (None, "stream"):
+            if path:
+                os.environ["PB_PATH"] = path
+            for logits, params in cases:
+                V = logits.shape[1]
+                lo, hi = V * rank // world, V * (rank + 1) // world
+                x = logits.cuda()
+                local = x[:, lo:hi].contiguous()
+                gens = [torch.Generator().manual_seed(i) for i in range(len(params))]
+                got = sample_tokens_vocab_parallel(local, params, gens)
+                gens = [torch.Generator().manual_seed(i) for i in range(len(params))]
+                want = sample_tokens(x, params, gens)
+                if got != want:
+                    bad = [i for i in range(len(got)) if got[i] != want[i]]
+                    print(f"rank {rank} ({path}): {len(bad)} rows differ, first {bad[:5]}", flush=True)
+                    ok = False
+            os.environ.pop("PB_PATH", None)
         flag = torch.tensor([0 if ok else 1], device="cuda")
         dist.all_reduce(flag)
         ok = int(flag.item()) == 0
