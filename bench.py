@@ -283,7 +283,7 @@ def device_config_measure(w, dev, stream, steps: int):
     out = {"us_per_step": step_ms * 1e3, "rows_per_s": B / (step_ms / 1e3),
            "per_launch_us": {"p50": pct(launches, 50), "p99": pct(launches, 99)},
            "hbm_frac": B * V * elem / (step_ms / 1e3) / 1e9 / peak,
-           "gpu_launches_per_step": L.pb_sample_launches(B, V, ops._DTYPE_CODE[w.logits.dtype], 0),
+           "gpu_launches_per_step": 2 if ops._ws_path() else L.pb_sample_launches(B, V, ops._DTYPE_CODE[w.logits.dtype], 0),
            "clocks": clocks, "config": workload_config(w)}
     del bufs
     torch.cuda.empty_cache()
@@ -424,6 +424,120 @@ def run_vocab_parallel(args):
         dist.destroy_process_group()
 
 
+# ---- config 4: the reference engine end to end ---------------------------------------------------
+
+def _cfg4_params(RefSP, i: int, rows: int = 256):
+    """Config 1's mix for request i of 256: greedy, temperature-only, top-k, top-p blocks of 64."""
+    q = rows // 4
+    blk, j = divmod(i, q)
+    kw = dict(max_tokens=256, ignore_eos=True, seed=i)
+    if blk == 0:
+        return RefSP(temperature=0.0, **kw)
+    if blk == 1:
+        return RefSP(temperature=(0.5, 1.0, 1.5)[j % 3], **kw)
+    if blk == 2:
+        return RefSP(temperature=1.0, top_k=(1, 20, 100, 1000)[j % 4], **kw)
+    return RefSP(temperature=1.0, top_p=(0.5, 0.9, 0.99)[j % 3], **kw)
+
+
+def engine_decode_config4(dev, steps_ours: int = 48, steps_ref: int = 6) -> dict:
+    """Config 4: the reference's LLMEngine (pagedbatch/engine.py) with its smollm2-135m-random model
+    (random weights, bf16, CUDA), 256 sequences, prompts of uniform-random token ids with lengths
+    uniform in [64, 512], 256 output tokens each (ignore_eos), block_size 16, sampling parameters
+    mixed as in config 1. Every prompt is prefilled first; then `steps_ours` decode steps run with
+    one batched launch per step (pagedbatch_b200.engine_hook) and `steps_ref` with the reference's
+    own per-row sample_token (sampling.py:10-27), each step timed between device synchronisations.
+    The sampling share is sampling time / step time (the step includes the model forward)."""
+    path = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "pagedbatch")):
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    import pagedbatch.engine as em
+    from pagedbatch.config import EngineConfig
+    from pagedbatch.config import SamplingParams as RefSP
+    from pagedbatch.loader import load_model
+
+    from pagedbatch_b200 import engine_hook
+
+    B, P_LO, P_HI = 256, 64, 512
+    model, mcfg, tok = load_model("smollm2-135m-random", device=str(dev), dtype="bfloat16", seed=0)
+    ecfg = EngineConfig(block_size=16, num_blocks=B * (P_HI + 256 + 16) // 16 + 64, max_num_seqs=B,
+                        max_num_batched_tokens=16384, max_model_len=1024, device=str(dev), dtype="bfloat16",
+                        seed=0)
+    eng = em.LLMEngine(model, mcfg, tok, ecfg)
+    rng = np.random.default_rng(0)
+    for i in range(B):
+        n = int(rng.integers(P_LO, P_HI + 1))
+        eng.add_request(prompt_token_ids=rng.integers(0, mcfg.vocab_size, n).tolist(),
+                        sampling=_cfg4_params(RefSP, i, B), request_id=f"r{i}")
+    engine_hook.install(eng)
+    t0 = time.perf_counter()
+    prefill_steps = 0
+    while any(not st.seq.output_token_ids for st in eng._requests.values()):
+        eng.step()
+        prefill_steps += 1
+    torch.cuda.synchronize(dev)
+    prefill_s = time.perf_counter() - t0
+
+    for _ in range(2):  # warm-up decode steps
+        eng.step()
+    st_o, sp_o = [], []
+    for _ in range(steps_ours):
+        before = engine_hook.stats.seconds
+        torch.cuda.synchronize(dev)
+        a = time.perf_counter()
+        eng.step()
+        torch.cuda.synchronize(dev)
+        st_o.append(time.perf_counter() - a)
+        sp_o.append(engine_hook.stats.seconds - before)
+    rows_step = len(eng._requests)
+    # the reference's per-row sampler on the same engine (its own sample_token, timed per call)
+    engine_hook.uninstall(eng)
+    engine_hook.restore_module(em)
+    ref_fn = em.sample_token
+    acc = [0.0]
+
+    def ref_timed(logits, params, generator):
+        a = time.perf_counter()
+        t = ref_fn(logits, params, generator)  # (.item() inside waits for the device)
+        acc[0] += time.perf_counter() - a
+        return t
+
+    em.sample_token = ref_timed
+    try:
+        st_r, sp_r = [], []
+        for _ in range(steps_ref):
+            acc[0] = 0.0
+            torch.cuda.synchronize(dev)
+            a = time.perf_counter()
+            eng.step()
+            torch.cuda.synchronize(dev)
+            st_r.append(time.perf_counter() - a)
+            sp_r.append(acc[0])
+    finally:
+        em.sample_token = ref_fn
+    med = statistics.median
+    out = {
+        "workload": "cfg4_smollm2-135m-random_bf16_256seq_decode",
+        "model": "smollm2-135m-random (30 layers, hidden 576, 9 heads, 3 KV heads, vocab 49152), bf16, random weights",
+        "sequences": B, "prompt_len": f"uniform [{P_LO}, {P_HI}]", "output_tokens": 256, "block_size": 16,
+        "sampling": "config 1 mix (64 greedy, 64 temperature-only, 64 top-k, 64 top-p), per-request seeds",
+        "prefill": {"steps": prefill_steps, "s": prefill_s},
+        "rows_per_decode_step": rows_step,
+        "ours": {"decode_steps": steps_ours, "step_ms": 1e3 * med(st_o), "sampling_ms": 1e3 * med(sp_o),
+                 "sampling_share": med(sp_o) / med(st_o),
+                 "api": "pagedbatch_b200.engine_hook.install (one sample_tokens launch per step)"},
+        "reference": {"decode_steps": steps_ref, "step_ms": 1e3 * med(st_r), "sampling_ms": 1e3 * med(sp_r),
+                      "sampling_share": med(sp_r) / med(st_r),
+                      "api": "pagedbatch.sampling.sample_token per row (engine.py:139), CUDA logits"},
+        "timing": "host clock around each engine.step() between torch.cuda.synchronize() calls; medians",
+    }
+    del eng, model
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---- our arm ----------------------------------------------------------------------------------
 
 def run_ours(args):
@@ -491,7 +605,9 @@ def run_ours(args):
     peak, peak_kind = load_peaks()
     alg_bytes = B * V * elem
     achieved = alg_bytes / (step_ms / 1e3) / 1e9
-    per_step_launches = L.pb_sample_launches(B, V, ops._DTYPE_CODE[w.logits.dtype], 0)
+    # pb_sample_ws (the default path): the balanced streaming kernel, then the cluster kernel over the
+    # rows it leaves; pb_sample: 1 or 2 launches by shape
+    per_step_launches = 2 if ops._ws_path() else L.pb_sample_launches(B, V, ops._DTYPE_CODE[w.logits.dtype], 0)
     line = {
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3, "higher_is_better": True,
@@ -532,6 +648,10 @@ def run_ours(args):
             extra[name] = device_config_measure(ew, dev, stream, args.steps)
             if not args.no_cpu_baseline:
                 extra[name]["cpu_baseline"] = cpu_baseline(ew, budget_s=3.0, min_rows=2)
+        try:
+            extra["cfg4"] = engine_decode_config4(dev)
+        except Exception as e:  # the line must still print; the reason is reported
+            extra["cfg4"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
         line["extra_configs"] = extra
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -2302,511 +2302,6 @@ __global__ void __launch_bounds__(MW_ROWS * 32) merge_warp_kernel(MergeArgs m) {
   }
 }
 
-// ---- persistent pass: the workspace path --------------------------------------------------------
-//
-// pb_sample_ws runs a batch as pass_kernel -> sample_kernel restricted to the rows the pass could
-// not settle. pass_kernel is persistent (at most two CTAs per SM, no clusters). A row's body of
-// 16-byte vectors is cut into `parts` units of at most `cpu` staged chunks; CTA g takes units
-// g, g + grid, g + 2 grid, ... and streams them through one TMA ring that runs on across unit
-// boundaries, so the copies of the next unit are in flight while a unit is closed. A unit leaves a
-// candidate record in the vocabulary-parallel format (a unit is a shard of its row); the CTA that
-// closes a row's last unit merges the row's records at once, with the arithmetic of the full-row
-// small path, while the other CTAs keep streaming.
-
-constexpr int U_CAP = 512;      // entries per unit record
-constexpr int U_KMAX = 256;     // largest top_k the pass resolves (the first threshold needs k <= 32 * NW)
-constexpr int U_MAXPARTS = 64;  // units per row
-constexpr int U_MAXCPU = 8;     // staged chunks per unit
-constexpr int U_MERGE = 4096;   // union entries one merge holds (16 per thread)
-static_assert(SLOTS * NT >= KCAP, "a merge's survivors reuse the candidate slots");
-static_assert(U_MERGE % NT == 0, "the union splits evenly");
-
-struct PassArgs {
-  const char* logits;
-  int64_t n_rows, vocab, row_stride;
-  const int32_t* row_index;
-  const pb_row_params* params;
-  int32_t cpu;         // staged chunks per unit
-  int32_t parts;       // units per row
-  int64_t units;       // n_rows * parts
-  uint32_t* row_done;  // units closed per row; zero when the launch starts, zero again when it ends
-  uint8_t* records;    // [n_rows][parts][record_bytes(U_CAP)]
-  int64_t* out_token;
-  pb_row_info* out_info;  // every row: settled, or PB_ROW_FALLBACK for the full-row kernel
-};
-
-enum : int { U_SKIP = 0, U_BAD = 1, U_GREEDY = 2, U_FILTER = 3 };
-
-// What the pass does with a row: settle rejected parameters, stream greedy rows and top-k rows with
-// k <= U_KMAX, leave every other row to the full-row kernel.
-__device__ __forceinline__ int unit_mode(const pb_row_params& p, int64_t V) {
-  const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
-  if (bad) return U_BAD;
-  if (p.temperature == 0.0) return U_GREEDY;
-  if (p.top_k > 0 && (int64_t)p.top_k < V && p.top_k <= U_KMAX) return U_FILTER;
-  return U_SKIP;
-}
-
-// Unit u of the batch: row item = u / parts, part = u % parts. Its vectors are [v0, v0 + nv) of the
-// row's 16-byte-aligned body (element vec_e0 onwards); part 0 also owns the scalar head, the last
-// part the scalar tail.
-template <typename T>
-struct UnitGeom {
-  int64_t item;
-  const T* row;
-  int64_t head_n, vec_e0, tail_e0, tail_n, e_first;
-  int32_t nv;
-  __device__ UnitGeom(const PassArgs& a, int64_t u) {
-    constexpr int ES = Elem<T>::ES, EPV = Elem<T>::EPV;
-    item = u / a.parts;
-    const int part = (int)(u - item * a.parts);
-    const int64_t V = a.vocab;
-    const int64_t row_id = a.row_index ? (int64_t)a.row_index[item] : item;
-    row = reinterpret_cast<const T*>(a.logits) + row_id * a.row_stride;
-    int64_t head = (int64_t)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / ES);
-    if (head > V) head = V;
-    const int64_t nvec_all = (V - head) / EPV;
-    const int64_t uv = (int64_t)a.cpu * (CHUNK_BYTES / 16);
-    const int64_t v0 = min(nvec_all, (int64_t)part * uv);
-    nv = (int32_t)(min(nvec_all, v0 + uv) - v0);
-    vec_e0 = head + v0 * EPV;
-    head_n = (part == 0) ? head : 0;
-    tail_e0 = head + nvec_all * EPV;
-    tail_n = (part == a.parts - 1) ? V - tail_e0 : 0;
-    e_first = (part == 0) ? 0 : vec_e0;
-  }
-};
-
-// Lower bound of a unit's top_k-th value from its first staged chunk: each warp's
-// ceil(top_k / NW)-th largest per-thread maximum, smallest over the warps (the NW warps then hold
-// at least top_k values at or above it; padding counts as -inf, which only lowers the bound).
-// Returns its tie floor. All threads call.
-template <int VPT>
-__device__ float unit_threshold(const float (&vm)[VPT], int top_k, float tf, Shared& sh) {
-  float mx = vm[0];
-#pragma unroll
-  for (int j = 1; j < VPT; ++j) mx = fmax_nan(mx, vm[j]);
-  const uint32_t lo = block_offer_bound(key_of(mx), top_k, sh);
-  __syncthreads();  // sh.red read by every thread
-  if (threadIdx.x == 0) sh.thr_f = (lo > KEY_NEG_INF) ? tie_floor(value_of(lo), tf) : -INFINITY;
-  __syncthreads();
-  return sh.thr_f;
-}
-
-// Merge one row from its units' records (the row's last unit was just closed by this CTA), with the
-// steps of merge_kernel: union of the survivors, exact top_k-th key, then finish_survivors. The
-// records are read through L2 only (other CTAs wrote them during this launch). K (KCAP entries)
-// holds the survivors. All threads call.
-__device__ void pass_merge(const PassArgs& a, int64_t item, const pb_row_params& p, uint64_t* K, Shared& sh) {
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int P = a.parts;
-  const int64_t rb = record_bytes(U_CAP);
-  const uint8_t* base = a.records + item * P * rb;
-  __shared__ uint32_t uoff[U_MAXPARTS + 1];
-  __shared__ int32_t w_fl[NW];
-  __shared__ float w_hm[NW], w_gk[NW];
-  __shared__ uint64_t w_gb[NW];
-
-  int32_t fl = 0, cnt = 0;
-  float hm = -INFINITY, gk = -INFINITY;
-  uint64_t gb = 0;
-  if (tid < P) {
-    const int4 h = __ldcg(reinterpret_cast<const int4*>(base + tid * rb));
-    cnt = h.x;
-    fl = h.y;
-    hm = __int_as_float(h.z);
-    if ((fl & PB_CAND_GREEDY) && cnt == 1) {
-      gb = __ldcg(reinterpret_cast<const unsigned long long*>(base + tid * rb + sizeof(pb_cand_header)));
-      gk = hm;
-    }
-  }
-  uint32_t total;
-  const uint32_t off = block_excl_scan<uint32_t, NT>((uint32_t)cnt, sh.s32, &total);
-  if (tid < P) uoff[tid] = off;
-  if (tid == 0) uoff[P] = total;
-  fl = (int32_t)__reduce_or_sync(0xFFFFFFFFu, (uint32_t)fl);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    hm = fmax_nan(hm, __shfl_xor_sync(0xFFFFFFFFu, hm, o));
-    const uint64_t gb2 = __shfl_xor_sync(0xFFFFFFFFu, gb, o);
-    const float gk2 = __shfl_xor_sync(0xFFFFFFFFu, gk, o);
-    if (gb2 > gb) {
-      gb = gb2;
-      gk = gk2;
-    }
-  }
-  if (lane == 0) {
-    w_fl[w] = fl;
-    w_hm[w] = hm;
-    w_gb[w] = gb;
-    w_gk[w] = gk;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    for (int i = 1; i < NW; ++i) {
-      fl |= w_fl[i];
-      hm = fmax_nan(hm, w_hm[i]);
-      if (w_gb[i] > gb) {
-        gb = w_gb[i];
-        gk = w_gk[i];
-      }
-    }
-    const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
-    const uint32_t mk = key_of(hm);
-    int mode = 0;  // 0 status only, 1 greedy, 2 merge
-    sh.status = PB_ROW_OK;
-    if (fl & PB_ROW_TIMEOUT) sh.status = PB_ROW_TIMEOUT;
-    else if (bad) sh.status = PB_ROW_BAD_PARAMS;
-    else if (p.temperature == 0.0) mode = 1;
-    else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) sh.status = PB_ROW_NONFINITE;
-    else if (!(p.uniform >= 0.0 && p.uniform < 1.0)) sh.status = PB_ROW_BAD_UNIFORM;
-    else if ((fl & (PB_CAND_FALLBACK | 0xFF)) || total > (uint32_t)U_MERGE || total == 0) sh.status = PB_ROW_FALLBACK;
-    else mode = 2;
-    if (mode == 1 && (fl & ~PB_CAND_GREEDY)) {  // a unit could not publish its maximum (a NaN)
-      sh.status = PB_ROW_FALLBACK;
-      mode = 0;
-    }
-    sh.nk = mode;
-    sh.row_max = hm;
-    sh.row_best = gk;
-    sh.arg = comp_idx(gb);
-  }
-  __syncthreads();
-  const int mode = sh.nk;
-  pb_row_info info = {};
-  int64_t token = -1;
-  info.status = sh.status;
-  if (mode == 1) {
-    info.max_key = sh.row_best;
-    info.thr_key = key_of(info.max_key);
-    info.n_tie_kept = 1;
-    info.kept_count = 1;
-    info.flags = PB_PATH_GREEDY;
-    token = sh.arg;
-  } else if (mode == 2) {
-    const float m = sh.row_max;
-    info.max_key = m;
-    auto entry = [&](uint32_t i) {  // union entry i (i < total): its unit is the last with uoff <= i
-      int lo = 0, hi = P;
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (uoff[mid] <= i) lo = mid;
-        else hi = mid;
-      }
-      return __ldcg(reinterpret_cast<const unsigned long long*>(base + lo * rb + sizeof(pb_cand_header)) +
-                    (i - uoff[lo]));
-    };
-    constexpr int NJ = U_MERGE / NT;
-    uint32_t kk[NJ];
-    uint32_t mn = 0xFFFFFFFFu, mx = 0;
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const uint32_t i = (uint32_t)(j * NT + tid);
-      kk[j] = (i < total) ? comp_key(entry(i)) : 0u;
-      if (i < total) mn = min(mn, kk[j]);
-      mx = max(mx, kk[j]);
-    }
-    uint32_t unused, kmin, kmax;
-    block_sum_min_max(0u, mn, mx, sh, &unused, &kmin, &kmax);
-    const uint32_t kq = (uint32_t)min((int64_t)p.top_k, (int64_t)total);
-    const uint32_t kth = block_kth_select<NJ>(kk, kq, kmin, total, (uint64_t)kmax + 1, true, sh);
-    if (tid == 0) sh.nk = 0;
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const uint32_t i = (uint32_t)(j * NT + tid);
-      const bool pass = i < total && kk[j] >= kth;
-      const uint32_t idx = pass ? comp_idx(entry(i)) : 0u;
-      warp_append(pass, kk[j], idx, K, &sh.nk, KCAP);
-    }
-    __syncthreads();
-    const int nk = sh.nk;
-    if (nk <= KCAP) {
-      const bool topp_active = p.top_p < 1.0 && (float)p.top_p < 1.0f;
-      finish_survivors(K, nk, m, topp_active, (float)p.top_p, (uint64_t)(p.uniform * 0x1p53), sh, &token, &info);
-    } else if (tid == 0) {
-      info.status = PB_ROW_FALLBACK;
-    }
-  } else if (sh.status == PB_ROW_NONFINITE || sh.status == PB_ROW_BAD_UNIFORM || sh.status == PB_ROW_TIMEOUT) {
-    info.max_key = sh.row_max;
-  }
-  if (tid == 0) {
-    a.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
-    pb_row_info* o = a.out_info + item;
-    o->thr_key = info.thr_key;
-    o->n_tie_kept = info.n_tie_kept;
-    o->kept_count = info.kept_count;
-    o->status = info.status;
-    o->max_key = info.max_key;
-    o->flags = info.flags;
-    o->z_q = info.z_q;
-    o->kept_q = info.kept_q;
-  }
-  __syncthreads();  // K and the shared scratch are free again
-}
-
-template <typename T>
-__global__ void __launch_bounds__(NT, 2) pass_kernel(PassArgs a) {
-  constexpr int EPV = Elem<T>::EPV;
-  constexpr int CV = CHUNK_BYTES / 16;  // vectors per chunk
-  constexpr int VPT = CV / NT;          // vectors per thread per chunk
-  constexpr int NSTAGE = RING_BYTES / CHUNK_BYTES;
-  extern __shared__ __align__(128) unsigned char dyn[];
-  __shared__ Shared sh;
-  __shared__ int32_t s_last;
-  __shared__ float lwf[NW], lwm[NW];
-  __shared__ uint32_t lwi[NW];
-  uint4* ring = reinterpret_cast<uint4*>(dyn);
-  uint64_t* slots = reinterpret_cast<uint64_t*>(dyn + RING_BYTES);
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int64_t G = gridDim.x;
-  const int64_t V = a.vocab;
-  const int cpu = a.cpu;
-  const int64_t my_units = (a.units - (int64_t)blockIdx.x + G - 1) / G;
-  const int64_t nseq = my_units * cpu;  // chunks this CTA walks (empty ones complete at once)
-
-  if (tid == 0) {
-    for (int st = 0; st < NSTAGE; ++st) {
-      mbar_init(&sh.mbar[st], 1);
-      sh.stage_chunk[st] = -1;
-      sh.released[st] = 0;
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  // stage chunk `seq` of this CTA's walk: a bulk copy, or an empty arrival when the unit has no
-  // such chunk or its row is not streamed
-  auto issue = [&](int64_t seq) {
-    const int st = (int)(seq % NSTAGE);
-    const int64_t i = seq / cpu;
-    const int cc = (int)(seq - i * cpu);
-    const UnitGeom<T> g(a, (int64_t)blockIdx.x + i * G);
-    const int mode = unit_mode(a.params[g.item], V);
-    const int n = (mode == U_GREEDY || mode == U_FILTER) ? max(0, min(CV, g.nv - cc * CV)) : 0;
-    sh.stage_chunk[st] = seq;
-    if (n > 0) {
-      mbar_expect_tx(&sh.mbar[st], (uint32_t)(n * 16));
-      bulk_load(ring + st * CV, reinterpret_cast<const uint4*>(g.row + g.vec_e0) + (int64_t)cc * CV, (uint32_t)(n * 16),
-                &sh.mbar[st], l2_policy_evict_first());
-    } else {
-      mbar_arrive(&sh.mbar[st]);
-    }
-  };
-  if (tid == 0)
-    for (int64_t s = 0; s < NSTAGE && s < nseq; ++s) issue(s);
-
-  bool timed_out = false;    // this warp gave up waiting (warp-uniform)
-  bool cta_timeout = false;  // some warp of the CTA gave up (CTA-uniform)
-  for (int64_t i = 0; i < my_units; ++i) {
-    const int64_t u = (int64_t)blockIdx.x + i * G;
-    const UnitGeom<T> g(a, u);
-    const pb_row_params p = a.params[g.item];
-    const int mode = unit_mode(p, V);
-    const bool greedy = mode == U_GREEDY, filtering = mode == U_FILTER;
-    const float tf = (float)p.temperature;
-    const int32_t top_k = p.top_k;
-    float runmax = -INFINITY, bestv = -INFINITY;
-    uint32_t bidx = 0xFFFFFFFFu;
-    int nc = 0;
-    bool ovf = false;
-    float t = -INFINITY;  // candidate threshold of this unit
-    auto push = [&](float x, uint32_t e) {
-      if (nc < SLOTS) {
-        slots[nc * NT + tid] = compose(key_of(x), e);
-        ++nc;
-      } else {
-        ovf = true;
-      }
-    };
-    const uint32_t e_base = (uint32_t)g.vec_e0 + (uint32_t)tid * EPV;
-    for (int cc = 0; cc < cpu; ++cc) {
-      const int64_t seq = i * cpu + cc;
-      const int stage = (int)(seq % NSTAGE);
-      const uint32_t parity = (uint32_t)((seq / NSTAGE) & 1);
-      if (!timed_out) timed_out = !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sh.mbar[stage], parity, WAIT_POLLS));
-      const int n = (greedy || filtering) ? max(0, min(CV, g.nv - cc * CV)) : 0;
-      const uint4* buf = ring + stage * CV;
-      float x[VPT][EPV];
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        if (j * NT + tid < n && !timed_out) {
-          Elem<T>::unpack(buf[j * NT + tid], x[j]);
-        } else {
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) x[j][q] = -INFINITY;
-        }
-      }
-      __syncwarp();
-      if (lane == 0 && !timed_out) {
-        // this warp is done with the stage; the last warp to release it refills it
-        if (atom_add_acq_rel(&sh.released[stage], 1u) == NW - 1) {
-          sh.released[stage] = 0;
-          if (seq + NSTAGE < nseq) {
-            fence_proxy_async();
-            issue(seq + NSTAGE);
-          }
-        }
-      }
-      if (n == 0) continue;  // the same for every thread
-      float vm[VPT];
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        float m2 = fmax_nan(x[j][0], x[j][1]);
-#pragma unroll
-        for (int q = 2; q < EPV; ++q) m2 = fmax_nan(m2, x[j][q]);
-        vm[j] = m2;
-        runmax = fmax_nan(runmax, m2);
-      }
-      if (greedy) {
-#pragma unroll
-        for (int j = 0; j < VPT; ++j) {
-          if (vm[j] > bestv) {
-            bestv = vm[j];
-            int jj = EPV - 1;
-#pragma unroll
-            for (int q = EPV - 1; q >= 0; --q)
-              if (x[j][q] == vm[j]) jj = q;
-            bidx = e_base + (uint32_t)((cc * CV + j * NT) * EPV + jj);
-          }
-        }
-      } else if (filtering) {
-        if (cc == 0) t = unit_threshold<VPT>(vm, top_k, tf, sh);
-#pragma unroll
-        for (int j = 0; j < VPT; ++j) {
-          if (j * NT + tid < n && vm[j] >= t) {
-            const uint32_t e0 = e_base + (uint32_t)((cc * CV + j * NT) * EPV);
-#pragma unroll
-            for (int q = 0; q < EPV; ++q)
-              if (x[j][q] >= t) push(x[j][q], e0 + q);
-          }
-        }
-      }
-    }
-    // scalar head (part 0) and tail (last part)
-    if ((greedy || filtering) && !cta_timeout) {
-      auto visit = [&](int64_t e) {
-        const float x = Elem<T>::ld(g.row + e);
-        runmax = fmax_nan(runmax, x);
-        if (greedy && x > bestv) {
-          bestv = x;
-          bidx = (uint32_t)e;
-        }
-        if (filtering && x >= t) push(x, (uint32_t)e);
-      };
-      for (int64_t e = tid; e < g.head_n; e += NT) visit(e);
-      for (int64_t e = tid; e < g.tail_n; e += NT) visit(g.tail_e0 + e);
-    }
-    if (__syncthreads_or(timed_out)) cta_timeout = true;
-    timed_out = cta_timeout;  // after a timeout no warp waits again
-    const bool unit_ovf = __syncthreads_or(ovf) != 0;
-    // CTA reduction: NaN-propagating max, first maximum
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bestv, o);
-      const uint32_t i2 = __shfl_xor_sync(0xFFFFFFFFu, bidx, o);
-      if (v2 > bestv || (v2 == bestv && i2 < bidx)) {
-        bestv = v2;
-        bidx = i2;
-      }
-      runmax = fmax_nan(runmax, __shfl_xor_sync(0xFFFFFFFFu, runmax, o));
-    }
-    if (lane == 0) {
-      lwf[tid >> 5] = bestv;
-      lwi[tid >> 5] = bidx;
-      lwm[tid >> 5] = runmax;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      if (lwf[w] > bestv || (lwf[w] == bestv && lwi[w] < bidx)) {
-        bestv = lwf[w];
-        bidx = lwi[w];
-      }
-      runmax = fmax_nan(runmax, lwm[w]);
-    }
-    __syncthreads();  // lwf/lwi/lwm are read before the next unit writes them
-
-    // this unit's record
-    uint8_t* rec = a.records + u * record_bytes(U_CAP);
-    pb_cand_header* hdr = reinterpret_cast<pb_cand_header*>(rec);
-    uint64_t* ent = reinterpret_cast<uint64_t*>(rec + sizeof(pb_cand_header));
-    int32_t h_count = 0, h_flags = 0;
-    float h_max = 0.0f;
-    if (cta_timeout) {
-      h_flags = PB_ROW_TIMEOUT;
-    } else if (mode == U_BAD) {
-      h_flags = PB_ROW_BAD_PARAMS;
-    } else if (mode == U_SKIP) {
-      h_flags = PB_CAND_FALLBACK;
-    } else if (greedy) {
-      h_max = bestv;
-      if (runmax != runmax) {
-        h_flags = PB_CAND_FALLBACK;  // a NaN: the full-row kernel finds the first one
-      } else {
-        h_flags = PB_CAND_GREEDY;
-        if (g.nv > 0 || g.head_n > 0 || g.tail_n > 0) {
-          // every value -inf: the unit's first index stands for its maximum
-          if (tid == 0) ent[0] = compose(key_of(bestv), (bidx == 0xFFFFFFFFu) ? (uint32_t)g.e_first : bidx);
-          h_count = 1;
-        }
-      }
-    } else {
-      const float m = __fdiv_rn(runmax, tf);
-      h_max = m;
-      if (key_of(m) >= KEY_POS_INF) {
-        h_flags = PB_ROW_NONFINITE;  // NaN or +inf: so is the whole row
-      } else if (unit_ovf) {
-        h_flags = PB_CAND_FALLBACK;
-      } else {
-        uint32_t tot;
-        uint32_t pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
-        if (tot > (uint32_t)U_CAP) {  // crowded: shrink to about this unit's top_k first
-          nc = compact_slots(slots, nc, top_k, tf, sh);
-          pos = block_excl_scan<uint32_t, NT>((uint32_t)nc, sh.s32, &tot);
-        }
-        if (tot <= (uint32_t)U_CAP) {
-          for (int j = 0; j < nc; ++j) {
-            const uint64_t cv = slots[j * NT + tid];
-            ent[pos + j] = compose(key_of(__fdiv_rn(value_of(comp_key(cv)), tf)), comp_idx(cv));
-          }
-          h_count = (int32_t)tot;
-        } else {
-          h_flags = PB_CAND_FALLBACK;
-        }
-      }
-    }
-    if (tid == 0) {
-      hdr->count = h_count;
-      hdr->flags = h_flags;
-      hdr->max_key = h_max;
-      hdr->reserved = 0;
-    }
-    // close the unit: the CTA that closes a row's last unit merges the row (the barrier orders the
-    // CTA's record writes before thread 0's device-scope fence and arrival)
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      const uint32_t done = atomicAdd(&a.row_done[g.item], 1u) + 1u;
-      const bool last = done == (uint32_t)a.parts;
-      if (last) {
-        a.row_done[g.item] = 0u;  // no other unit of this row is left in this launch
-        __threadfence();
-      }
-      s_last = last ? 1 : 0;
-    }
-    __syncthreads();
-    if (s_last) pass_merge(a, g.item, p, slots, sh);
-  }
-  if (cta_timeout && tid == 0) {
-    // let every issued copy land before the CTA leaves
-    for (int st = 0; st < NSTAGE; ++st) {
-      const int64_t c = sh.stage_chunk[st];
-      if (c >= 0) mbar_wait_bounded(&sh.mbar[st], (uint32_t)((c / NSTAGE) & 1), WAIT_POLLS);
-    }
-  }
-}
-
 // Per-device one-time set-up (a function attribute, a device property): a bit per device, set
 // atomically, so that concurrent first calls from several host threads are safe (the set-up itself
 // is idempotent).
@@ -2871,7 +2366,7 @@ int launch(const Args& a, int C, cudaStream_t stream, bool pdl = false) {
 
 // The persistent streaming kernel: one CTA per SM (at most one per row).
 template <typename T>
-int launch_stream(const FastArgs& a, cudaStream_t stream) {
+int launch_stream(const FastArgs& a, int64_t grid, cudaStream_t stream) {
   static DeviceOnce configured;
   int dev = 0;
   if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
@@ -2880,7 +2375,6 @@ int launch_stream(const FastArgs& a, cudaStream_t stream) {
       return PB_E_DEVICE;
     configured.set(dev);
   }
-  const int64_t grid = std::min<int64_t>(a.n_rows, sm_count());
   stream_kernel<T><<<(unsigned)grid, F_THREADS, F_SMEM, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
   return PB_OK;
@@ -2939,122 +2433,59 @@ int launch_merge(const uint8_t* records, int32_t n_shards, int64_t n_rows, int32
   return PB_OK;
 }
 
-constexpr int PASS_SMEM = RING_BYTES + SLOTS * NT * 8;
-
-// Resident pass CTAs per SM (the grid is one wave of them); 1 when the query fails.
-int pass_ctas_per_sm(int es) {
-  static DeviceInt occ[2];
-  int dev = 0;
-  if (current_device(&dev) != PB_OK) dev = 0;
-  const int which = (es == 4) ? 0 : 1;
-  int have = occ[which].v[dev].load(std::memory_order_relaxed);
-  if (!have) {
-    int n = 0;
-    cudaError_t rc;
-    if (es == 4) {
-      cudaFuncSetAttribute(pass_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
-      rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pass_kernel<float>, NT, PASS_SMEM);
-    } else {
-      cudaFuncSetAttribute(pass_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
-      cudaFuncSetAttribute(pass_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, PASS_SMEM);
-      rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pass_kernel<__nv_bfloat16>, NT, PASS_SMEM);
-    }
-    have = (rc == cudaSuccess && n > 0) ? n : 1;
-    occ[which].v[dev].store(have, std::memory_order_relaxed);
-  }
-  return have;
-}
-
-// Geometry of a pass launch: staged chunks per unit, units per row, total units, grid.
-struct PassPlan {
-  int cpu = 0, parts = 0;
-  int64_t units = 0, grid = 0;
-};
-
-// The unit size that minimises the busiest CTA's walk: rounds of units times (chunks per unit plus
-// half a chunk for closing the unit), over a grid of one wave of resident CTAs. A row may be cut into at most
-// U_MAXPARTS units; a vocabulary too long for that has no plan (the full-row kernel takes the batch).
-bool pass_plan(int64_t n_rows, int64_t vocab, int es, PassPlan* out) {
-  if (n_rows <= 0 || vocab <= 0) return false;
-  const int64_t epv = 16 / es, cv = CHUNK_BYTES / 16;
-  const int64_t nvec_max = vocab / epv;  // no row has more body vectors
-  const int64_t cap = (int64_t)pass_ctas_per_sm(es) * sm_count();
-  int lo = 1, hi = U_MAXCPU;
-  if (const char* env = getenv("PB_PASS_CPU")) {
-    const int c = atoi(env);
-    if (c >= 1 && c <= U_MAXCPU) lo = hi = c;
-  }
-  double best = 0.0;
-  bool found = false;
-  for (int cpu = hi; cpu >= lo; --cpu) {
-    const int64_t parts = std::max<int64_t>(1, (nvec_max + cpu * cv - 1) / (cpu * cv));
-    if (parts > U_MAXPARTS) continue;
-    const int64_t units = n_rows * parts;
-    const int64_t grid = std::min(units, cap);
-    const int64_t rounds = (units + grid - 1) / grid;
-    const double cost = (double)rounds * (cpu + 0.5);
-    if (!found || cost < best) {
-      best = cost;
-      found = true;
-      out->cpu = cpu;
-      out->parts = (int)parts;
-      out->units = units;
-      out->grid = grid;
-    }
-  }
-  return found;
-}
-
 constexpr int64_t align256(int64_t n) { return (n + 255) & ~(int64_t)255; }
 
-// workspace of pb_sample_ws: per-row unit counters, per-row info, then the unit records
-int64_t ws_bytes_for(int64_t n_rows, const PassPlan& pl) {
-  return align256(n_rows * 4) + align256(n_rows * (int64_t)sizeof(pb_row_info)) + pl.units * record_bytes(U_CAP);
-}
+int stage_poll_limit();
 
-template <typename T>
-int launch_pass(const PassArgs& a, int grid, cudaStream_t stream) {
-  static DeviceOnce configured;
-  int dev = 0;
-  if (current_device(&dev) != PB_OK) return PB_E_DEVICE;
-  const int smem = PASS_SMEM;
-  if (!configured.test(dev)) {
-    if (cudaFuncSetAttribute(pass_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return PB_E_DEVICE;
-    configured.set(dev);
+// Balanced streaming launch (the workspace path): CTAs, at most one per SM, each share at least
+// SEG_MIN vectors long (so no share is empty).
+// PB_BALANCED_GRID caps the grid (tests use it to vary how rows are cut into pieces).
+int64_t balanced_grid(int64_t n_rows, int64_t vocab, int es) {
+  const int64_t epv = 16 / es;
+  const int64_t N = n_rows * ((vocab + epv - 1) / epv);
+  int64_t g = std::min<int64_t>((int64_t)F_CPS * sm_count(), N / SEG_MIN);
+  if (const char* env = getenv("PB_BALANCED_GRID")) {
+    const int64_t cap = atoll(env);
+    if (cap >= 1) g = std::min(g, cap);
   }
-  pass_kernel<T><<<(unsigned)grid, NT, smem, stream>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
-  return PB_OK;
+  return std::max<int64_t>(1, g);
 }
 
-// pass -> full-row kernel on the rows the pass left as PB_ROW_FALLBACK (see pb_sample_ws)
-int run_pass(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
-             const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
-             uint8_t* workspace, const PassPlan& pl, cudaStream_t st) {
-  uint32_t* row_done = reinterpret_cast<uint32_t*>(workspace);
-  pb_row_info* info =
-      out_info ? out_info : reinterpret_cast<pb_row_info*>(workspace + align256(n_rows * 4));
-  uint8_t* records = workspace + align256(n_rows * 4) + align256(n_rows * (int64_t)sizeof(pb_row_info));
-  if (cudaMemsetAsync(row_done, 0, (size_t)n_rows * 4, st) != cudaSuccess) return PB_E_LAUNCH;
-  PassArgs pa;
-  pa.logits = static_cast<const char*>(logits);
-  pa.n_rows = n_rows;
-  pa.vocab = vocab;
-  pa.row_stride = row_stride;
-  pa.row_index = row_index;
-  pa.params = params;
-  pa.cpu = pl.cpu;
-  pa.parts = pl.parts;
-  pa.units = pl.units;
-  pa.row_done = row_done;
-  pa.records = records;
-  pa.out_token = out_token;
-  pa.out_info = info;
-  int rc = (dtype == PB_DTYPE_F32)    ? launch_pass<float>(pa, (int)pl.grid, st)
-           : (dtype == PB_DTYPE_BF16) ? launch_pass<__nv_bfloat16>(pa, (int)pl.grid, st)
-                                      : launch_pass<__half>(pa, (int)pl.grid, st);
+// workspace of the balanced launch: per-row arrival counters, then one record per piece (a piece is
+// indexed by row + CTA, so n_rows + grid records cover every piece)
+int64_t ws_need(int64_t n_rows, int64_t grid) {
+  return align256(n_rows * 8) + (n_rows + grid) * record_bytes(F_SREC);
+}
+
+// balanced streaming kernel -> cluster kernel over the rows it did not take or could not settle
+template <typename T>
+int run_balanced(const Args& a, uint8_t* workspace, int64_t grid, int es, cudaStream_t st) {
+  FastArgs f;
+  f.logits = a.logits;
+  f.n_rows = a.n_rows;
+  f.vocab = a.vocab;
+  f.row_stride = a.row_stride;
+  f.row_index = a.row_index;
+  f.params = a.params;
+  f.out_token = a.out_token;
+  f.out_info = a.out_info;
+  f.cand_out = nullptr;
+  f.cand_cap = 0;
+  f.vocab_offset = 0;
+  f.poll_limit = stage_poll_limit();
+  f.balanced = 1;
+  f.row_cnt = reinterpret_cast<unsigned long long*>(workspace);
+  f.seg_rec = workspace + align256(a.n_rows * 8);
+  int rc = launch_stream<T>(f, grid, st);
   if (rc != PB_OK) return rc;
+  Args c = a;
+  c.complement = 1;
+  return launch<T>(c, cluster_size_for(a.n_rows, a.vocab, es), st, getenv("PB_NO_PDL") == nullptr);
+}
+
+int run_ws(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
+           const int32_t* row_index, const pb_row_params* params, int64_t* out_token, pb_row_info* out_info,
+           uint8_t* workspace, int64_t grid, cudaStream_t st) {
   Args a;
   a.logits = static_cast<const char*>(logits);
   a.n_rows = n_rows;
@@ -3065,15 +2496,14 @@ int run_pass(const void* logits, int dtype, int es, int64_t n_rows, int64_t voca
   a.out_token = out_token;
   a.out_info = out_info;
   a.out_probs = nullptr;
-  a.only_fallback = info;
+  a.only_fallback = nullptr;
   a.complement = 0;
   a.cand_out = nullptr;
   a.cand_cap = 0;
   a.vocab_offset = 0;
-  const int C = cluster_size_for(n_rows, vocab, es);
-  if (dtype == PB_DTYPE_F32) return launch<float>(a, C, st);
-  if (dtype == PB_DTYPE_BF16) return launch<__nv_bfloat16>(a, C, st);
-  return launch<__half>(a, C, st);
+  if (dtype == PB_DTYPE_F32) return run_balanced<float>(a, workspace, grid, es, st);
+  if (dtype == PB_DTYPE_BF16) return run_balanced<__nv_bfloat16>(a, workspace, grid, es, st);
+  return run_balanced<__half>(a, workspace, grid, es, st);
 }
 
 // ---- allocation-free entry point -------------------------------------------------------------
@@ -3145,7 +2575,10 @@ int run_rows(Args a, int es, cudaStream_t st) {
   f.cand_cap = a.cand_cap;
   f.vocab_offset = a.vocab_offset;
   f.poll_limit = stage_poll_limit();
-  int rc = launch_stream<T>(f, st);
+  f.balanced = 0;
+  f.row_cnt = nullptr;
+  f.seg_rec = nullptr;
+  int rc = launch_stream<T>(f, std::min<int64_t>(a.n_rows, (int64_t)F_CPS * sm_count()), st);
   if (rc != PB_OK) return rc;
   a.complement = 1;
   return launch<T>(a, C, st, getenv("PB_NO_PDL") == nullptr);
@@ -3243,9 +2676,7 @@ int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap,
 int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype) {
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
-  PassPlan pl;
-  if (!pass_plan(n_rows, vocab, es, &pl)) return 256;  // such a batch runs the full-row kernel
-  return ws_bytes_for(n_rows, pl);
+  return ws_need(n_rows, (int64_t)F_CPS * sm_count());  // (the grid never exceeds F_CPS CTAs per SM)
 }
 
 int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
@@ -3263,13 +2694,10 @@ int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, i
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
-  PassPlan pl;
-  if (!pass_plan(n_rows, vocab, es, &pl))
-    return pb_sample(logits, dtype, n_rows, vocab, row_stride, row_index, params, out_token, out_info, nullptr,
-                     stream);
-  if (ws_bytes < ws_bytes_for(n_rows, pl)) return PB_E_INVALID;
-  return run_pass(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
-                  static_cast<uint8_t*>(workspace), pl, static_cast<cudaStream_t>(stream));
+  const int64_t grid = balanced_grid(n_rows, vocab, es);
+  if (ws_bytes < ws_need(n_rows, grid)) return PB_E_INVALID;
+  return run_ws(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
+                static_cast<uint8_t*>(workspace), grid, static_cast<cudaStream_t>(stream));
 }
 
 int64_t pb_sample_noalloc_max_bytes(void) { return NOALLOC_SCRATCH_BYTES; }
@@ -3285,18 +2713,15 @@ int pb_sample_noalloc(const void* logits, int dtype, int64_t n_rows, int64_t voc
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
-  PassPlan pl;
-  if (!pass_plan(n_rows, vocab, es, &pl))  // the full-row kernel needs no workspace
-    return pb_sample(logits, dtype, n_rows, vocab, row_stride, row_index, params, out_token, out_info, nullptr,
-                     stream);
-  if (ws_bytes_for(n_rows, pl) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
+  const int64_t grid = balanced_grid(n_rows, vocab, es);
+  if (ws_need(n_rows, grid) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
   uint8_t* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != PB_OK) return rc;
-  // run_pass clears the per-row unit counters (a stream-ordered memset); every other byte the
-  // launches read is written earlier in the same call
-  return run_pass(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info, scratch, pl,
-                  static_cast<cudaStream_t>(stream));
+  // the launches need no cleared memory: the arrival counters carry a check word (see f_arrive) and
+  // every record is written before it is read
+  return run_ws(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info, scratch,
+                grid, static_cast<cudaStream_t>(stream));
 }
 
 uint32_t pb_key_of(float x) {

@@ -48,19 +48,19 @@ def params_tensor(rec: np.ndarray, device, pinned: bool = True) -> torch.Tensor:
 _WS: dict = {}
 
 
-def _pass_path() -> bool:
-    """The single full-row launch (default) or, with PB_PATH=pass, the persistent pass + fallback launches."""
-    return os.environ.get("PB_PATH", "full") == "pass"
+def _ws_path() -> bool:
+    """pb_sample (the default; measured faster at the benchmark's shapes) or, with PB_PATH=ws, tokens
+    without probabilities through pb_sample_ws (the balanced streaming launch over a workspace)."""
+    return os.environ.get("PB_PATH", "full") == "ws"
 
 
-def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-device scratch for pb_sample_ws, grown on demand (torch allocations are 256-byte aligned).
-
-    Launches on one device are stream-ordered; a caller that samples on several streams of the same
-    device at once must not share this buffer."""
+def _workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Scratch for pb_sample_ws, one buffer per (device, stream), grown on demand (torch allocations
+    are 256-byte aligned; the launches need no cleared memory). Calls on one stream are ordered, so
+    they share its buffer; calls on different streams get different buffers."""
     if nbytes < 0:
         raise ValueError("bad workspace request")
-    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), stream)
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
@@ -92,11 +92,11 @@ def _launch(logits: torch.Tensor, params: torch.Tensor, row_index, with_info: bo
     info = torch.empty((n, _lib.ROW_INFO.itemsize), dtype=torch.uint8, device=dev) if with_info else None
     probs = torch.empty((n, V), dtype=torch.float32, device=dev) if with_probs else None
     L = _lib.load()
-    if not with_probs and _pass_path():
+    if not with_probs and _ws_path():
         with torch.cuda.device(dev):
             need = L.pb_sample_ws_bytes(n, V, _DTYPE_CODE[logits.dtype])
-            ws = _workspace(dev, need)
             stream = torch.cuda.current_stream(dev).cuda_stream
+            ws = _workspace(dev, stream, need)
             rc = L.pb_sample_ws(
                 ctypes.c_void_p(logits.data_ptr()), _DTYPE_CODE[logits.dtype], n, V, logits.stride(0),
                 ctypes.c_void_p(row_index.data_ptr()) if row_index is not None else None,

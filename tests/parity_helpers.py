@@ -28,10 +28,25 @@ def _check(g_tok, g_info, o_tok, o_info, label):
     assert np.array_equal(g_info["max_key"], o_info["max_key"], equal_nan=True), label
 
 
+def _run_with_path(dev, rec, row_index, path):
+    """Tokens and info through one launch path (PB_PATH as the ops layer and the library read it)."""
+    old = os.environ.get("PB_PATH")
+    os.environ["PB_PATH"] = path
+    try:
+        return run_gpu(dev, rec, row_index, False)
+    finally:
+        if old is None:
+            os.environ.pop("PB_PATH", None)
+        else:
+            os.environ["PB_PATH"] = old
+
+
 def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""):
-    """GPU against the oracle. With probs, the launch that writes probabilities (the cluster kernel
-    alone) is checked, and then the same rows without probabilities through the streaming kernel
-    (then the cluster kernel on the rows it leaves)."""
+    """GPU against the oracle. With probs: the launch that writes probabilities (the cluster kernel
+    alone), then the same rows without probabilities through pb_sample's streaming kernel (whole
+    rows per CTA) and through pb_sample_ws (the balanced streaming launch, rows cut into pieces),
+    each followed by the cluster kernel on the rows it leaves. Without probs: the path PB_PATH
+    selects (pb_sample_ws by default)."""
     dev = logits_cpu.to(device)
     g_tok, g_info, g_pr = run_gpu(dev, rec, row_index, probs)
     o_tok, o_info, o_pr = oracle.sample(logits_cpu, rec, row_index, want_probs=probs)
@@ -41,16 +56,9 @@ def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""
         same = g_pr[ok].view(np.uint32) == o_pr[ok].view(np.uint32)
         rows_bad = np.flatnonzero(~same.all(axis=1))
         assert rows_bad.size == 0, f"{label}: probs differ on rows {rows_bad[:10]}"
-        # and the streaming kernel first (the default for batches with several rows per SM)
-        forced = "PB_PATH" not in os.environ
-        if forced:
-            os.environ["PB_PATH"] = "stream"
-        try:
-            s_tok, s_info, _ = run_gpu(dev, rec, row_index, False)
-        finally:
-            if forced:
-                os.environ.pop("PB_PATH", None)
-        _check(s_tok, s_info, o_tok, o_info, label + " (streaming kernel)")
+        for path in ("stream", "ws"):
+            s_tok, s_info, _ = _run_with_path(dev, rec, row_index, path)
+            _check(s_tok, s_info, o_tok, o_info, f"{label} ({path} path)")
     return g_tok, g_info
 
 

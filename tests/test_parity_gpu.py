@@ -24,7 +24,7 @@ pytestmark = pytest.mark.gpu
 def _need_cuda(cuda):
     yield
     os.environ.pop("PB_CLUSTER", None)
-    os.environ.pop("PB_PASS_CPU", None)
+    os.environ.pop("PB_BALANCED_GRID", None)
     os.environ.pop("PB_PATH", None)
 
 
@@ -269,63 +269,73 @@ def test_vocab_parallel_api_one_rank_nccl():
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cpu", ["1", "2", "4", "8"])
-def test_pass_path_modes_and_edges(cpu):
-    """The persistent pass + fallback launches (pb_sample_ws) against the oracle, several unit sizes."""
-    os.environ["PB_PATH"] = "pass"
-    os.environ["PB_PASS_CPU"] = cpu
-    rng = np.random.default_rng(20 + int(cpu))
+@pytest.mark.parametrize("grid", ["1", "3", "16", "148"])
+def test_balanced_path_modes_and_edges(grid):
+    """pb_sample_ws (balanced streaming launch + cluster kernel on the rest) against the oracle, with
+    the grid capped so rows are cut into different numbers of pieces."""
+    os.environ["PB_PATH"] = "ws"
+    os.environ["PB_BALANCED_GRID"] = grid
+    rng = np.random.default_rng(20 + int(grid))
     for V in (1, 3, 17, 258, 4099, 49152, 128256):
         B = 24
         x = workloads.head_boosted(B, V, seed=V)
         t = rng.choice([0.0, 0.5, 0.7, 1.0, 1.5], B)
-        k = rng.choice([0, 1, 2, 20, 50, 512, 513, 1000, max(1, V - 1), V], B)
+        k = rng.choice([0, 1, 2, 20, 50, 128, 129, 512, 1000, max(1, V - 1), V], B)
         p = rng.choice([1.0, 0.5, 0.9, 0.99, 1e-6], B)
         u = rng.random(B)
         u[:2] = [0.0, np.nextafter(1.0, 0.0)]
-        compare(x, oracle.make_params(t, p, k, u), probs=False, label=f"pass cpu={cpu} V={V}")
-    x = torch.randn(7, 600)
+        compare(x, oracle.make_params(t, p, k, u), probs=False, label=f"balanced grid={grid} V={V}")
+    x = torch.randn(7, 60000)
     x[0, 5] = float("nan")
-    x[1, 7] = float("inf")
+    x[1, 40007] = float("inf")
     x[2, :] = float("-inf")
     x[3, 300:] = float("-inf")
     x[4, :] = 1.0
     x[6, 100:] = float("-inf")
+    x[6, 59000] = float("nan")
     rec = oracle.make_params([1.0, 1.0, 1.0, 1.0, 0.0, 1.0, 0.0], [1.0] * 7, [10, 10, 10, 10, 0, 10, 0], [0.5] * 7)
     rec["uniform"][5] = 1.0
-    compare(x, rec, probs=False, label=f"pass nonfinite cpu={cpu}")
-    x2 = torch.tensor([[1.0, float("nan"), 3.0, float("nan")], [float("-inf")] * 4, [-0.0, 0.0, -1.0, 0.0]])
-    compare(x2, oracle.make_params([0.0] * 3, [1.0] * 3, [0] * 3, [0.0] * 3), probs=False, label="pass greedy edge")
+    compare(x, rec, probs=False, label=f"balanced nonfinite grid={grid}")
+    x2 = torch.full((4, 40000), float("-inf"))
+    x2[0, 1] = float("nan")
+    x2[0, 30000] = float("nan")
+    x2[2] = 0.0
+    x2[2, ::2] = -0.0
+    x2[3, 39999] = 2.0
+    x2[3, 20000] = 2.0
+    compare(x2, oracle.make_params([0.0] * 4, [1.0] * 4, [0] * 4, [0.0] * 4), probs=False,
+            label=f"balanced greedy edge grid={grid}")
     rec = oracle.make_params([-1.0, 1.0, 1.0, float("nan")], [1.0, 0.0, 1.5, 1.0], [0, 0, 0, 0], [0.5] * 4)
-    compare(torch.randn(4, 100), rec, probs=False, label="pass bad params")
+    compare(torch.randn(4, 100), rec, probs=False, label="balanced bad params")
 
 
-def test_pass_path_configs_and_row_index():
-    os.environ["PB_PATH"] = "pass"
-    for w in (workloads.config0(), workloads.config1(), workloads.config2()):
-        compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label=f"pass {w.name}")
-    # many units per CTA: each CTA walks a dozen or more units and merges several rows
-    for B, V in ((400, 128256), (3000, 4099)):
+def test_balanced_path_configs_and_row_index():
+    os.environ["PB_PATH"] = "ws"
+    for w in (workloads.config0(), workloads.config1(), workloads.config2(), workloads.config3(rows=300)):
+        compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label=f"balanced {w.name}")
+    # many rows per CTA, and rows cut into many pieces
+    for B, V in ((400, 128256), (3000, 4099), (2, 128256), (1, 1 << 20)):
         rng = np.random.default_rng(B)
         x = workloads.head_boosted(B, V, seed=B)
         t = rng.choice([0.0, 0.7, 1.0], B)
-        k = rng.choice([1, 20, 50, 256, 257], B)
+        k = rng.choice([1, 20, 50, 128, 129], B)
         p = rng.choice([1.0, 0.9, 0.95], B)
-        compare(x, oracle.make_params(t, p, k, rng.random(B)), probs=False, label=f"pass B={B} V={V}")
-    # rising values: the first chunk's threshold admits every later value, units overflow and the
-    # rows fall back to the full-row kernel
+        compare(x, oracle.make_params(t, p, k, rng.random(B)), probs=False, label=f"balanced B={B} V={V}")
+    # rising values: the first chunk's threshold admits every later value, pieces overflow and the
+    # rows fall back to the cluster kernel
     x = torch.arange(6 * 70000, dtype=torch.float32).reshape(6, 70000) % 70001
-    compare(x, oracle.make_params([1.0] * 6, [0.9] * 6, [50] * 6, [0.3] * 6), probs=False, label="pass rising")
+    compare(x, oracle.make_params([1.0] * 6, [0.9] * 6, [50] * 6, [0.3] * 6), probs=False, label="balanced rising")
     w = workloads.config1(rows=32)
     sel = np.array([31, 0, 5, 5, 17, 2, 30], np.int32)
     rec = rec_for([w.params[i] for i in sel], [w.uniforms()[i] for i in sel])
-    compare(w.logits, rec, sel, probs=False, label="pass row_index")
-    os.environ.pop("PB_PATH")
+    compare(w.logits, rec, sel, probs=False, label="balanced row_index")
+    os.environ["PB_PATH"] = "full"
     compare(w.logits, rec, sel, probs=False, label="full row_index")
+    os.environ.pop("PB_PATH")
 
 
-def test_pass_path_ties_and_sparse_rows():
-    os.environ["PB_PATH"] = "pass"
+def test_balanced_path_ties_and_sparse_rows():
+    os.environ["PB_PATH"] = "ws"
     V = 20000
     x = torch.zeros(6, V)
     x[1, ::3] = 1.0
@@ -334,20 +344,20 @@ def test_pass_path_ties_and_sparse_rows():
     x[4] = (torch.arange(V) % 7).float()
     x[5, :] = -1.0
     rng = np.random.default_rng(13)
-    for t, k, p in [(0.5, 500, 1.0), (1.0, 7, 0.99), (0.0, 0, 1.0), (1.0, 1, 1.0), (1.0, 300, 0.3)]:
-        for cpu in ("1", "4"):
-            os.environ["PB_PASS_CPU"] = cpu
+    for t, k, p in [(0.5, 500, 1.0), (1.0, 7, 0.99), (0.0, 0, 1.0), (1.0, 1, 1.0), (1.0, 100, 0.3)]:
+        for grid in ("1", "4"):
+            os.environ["PB_BALANCED_GRID"] = grid
             compare(x, oracle.make_params([t] * 6, [p] * 6, [k] * 6, rng.random(6)), probs=False,
-                    label=f"pass ties t={t} k={k} cpu={cpu}")
-    V = 4099
+                    label=f"balanced ties t={t} k={k} grid={grid}")
+    V = 40990
     x = torch.full((4, V), float("-inf"))
     for r, n in enumerate((1, 37, 500, 999)):
         cols = torch.from_numpy(rng.choice(V, n, replace=False))
         x[r, cols] = torch.randn(n, generator=torch.Generator().manual_seed(r)) * 2.0
-    rec = oracle.make_params([1.0, 0.7, 1.0, 1.3], [1.0, 0.9, 1.0, 0.5], [400, 400, 400, 400], rng.random(4))
-    for cpu in ("1", "8"):
-        os.environ["PB_PASS_CPU"] = cpu
-        compare(x, rec, probs=False, label=f"pass sparse-finite cpu={cpu}")
+    rec = oracle.make_params([1.0, 0.7, 1.0, 1.3], [1.0, 0.9, 1.0, 0.5], [100, 100, 128, 100], rng.random(4))
+    for grid in ("1", "8"):
+        os.environ["PB_BALANCED_GRID"] = grid
+        compare(x, rec, probs=False, label=f"balanced sparse-finite grid={grid}")
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

@@ -159,3 +159,24 @@ def test_bounded_wait_gives_up_and_reports_timeout():
     torch.cuda.synchronize()
     tok, info, _ = run_gpu(x, rec, probs=False)
     _check(tok, info, o_tok, o_info, "after timeout")
+
+
+def test_balanced_bounded_wait_gives_up_and_reports_timeout():
+    """The same with pb_sample_ws, whose rows are cut into pieces over neighbouring CTAs: a piece whose
+    CTA gave up still arrives (with a timed-out record), so every split row reports PB_ROW_TIMEOUT,
+    its arrival counter completes, and the next call (normal waits) over the same workspace is right."""
+    os.environ["PB_PATH"] = "ws"
+    w = workloads.config1(rows=64)
+    rec = rec_for(w.params, w.uniforms())
+    x = w.logits.cuda()
+    os.environ["PB_TEST_STAGE_POLLS"] = "0"
+    tok, info, _ = run_gpu(x, rec, probs=False)
+    el = _eligible(rec, x.shape[1])
+    assert np.all(info["status"][el] == _lib.ROW_TIMEOUT) and np.all(tok[el] == -1)
+    o_tok, o_info, _ = oracle.sample(w.logits, rec)
+    assert np.array_equal(tok[~el], o_tok[~el])
+    os.environ.pop("PB_TEST_STAGE_POLLS")
+    torch.cuda.synchronize()
+    for _ in range(2):
+        tok, info, _ = run_gpu(x, rec, probs=False)
+        _check(tok, info, o_tok, o_info, "balanced, after timeout")

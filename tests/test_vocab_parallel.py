@@ -171,3 +171,53 @@ def test_candidates_rejects_bad_cap(bad):
     L = _lib.load()
     rc = L.pb_candidates(None, 0, 1, 10, 10, None, None, 0, bad, None, None)
     assert rc == -1  # PB_E_INVALID, returned before any device work
+
+
+def _worker_fail(rank, port, q, mode):
+    """Two steps; between them rank 1 leaves ("exit") or stalls past the group's timeout ("stall").
+    Rank 0's second step must end with an error, not hang."""
+    import datetime
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=4))
+    x, params = _rows()
+    local = (x[:, :SPLIT] if rank == 0 else x[:, SPLIT:]).contiguous()
+    kern = OracleKernels(x.numpy())
+    gens = [torch.Generator().manual_seed(i) for i in range(B)]
+    sample_tokens_vocab_parallel(local, params, gens, kernels=kern)  # step 1, every rank
+    if rank == 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()  # (os._exit below skips the queue's flush)
+        if mode == "stall":
+            time.sleep(12)  # (longer than the group's timeout; no collective in flight)
+        os._exit(0)  # between steps: nothing of this rank is in flight
+    t0 = time.monotonic()
+    try:
+        sample_tokens_vocab_parallel(local, params, gens, kernels=kern)
+        q.put((rank, "returned", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001 - any error ends the step; the test reads its kind
+        q.put((rank, f"raised {type(e).__name__}", time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_surviving_rank_raises_when_a_peer_leaves(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_fail, args=(r, port, q, mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict((r, (what, dt)) for r, what, dt in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert got[1][0] == "left"
+    what, dt = got[0]
+    assert what.startswith("raised"), what
+    assert dt < 60.0
