@@ -499,8 +499,11 @@ def engine_decode_config4(dev, steps_ours: int = 48, steps_ref: int = 6) -> dict
     acc = [0.0]
 
     def ref_timed(logits, params, generator):
+        # the reference's request generators are CPU generators (engine.py:58,84), which
+        # torch.multinomial refuses for CUDA probabilities (sampling.py:27): the row is copied to the
+        # host first, inside the timed call, as a CUDA engine running this sampler has to
         a = time.perf_counter()
-        t = ref_fn(logits, params, generator)  # (.item() inside waits for the device)
+        t = ref_fn(logits.cpu(), params, generator)
         acc[0] += time.perf_counter() - a
         return t
 
@@ -530,7 +533,8 @@ def engine_decode_config4(dev, steps_ours: int = 48, steps_ref: int = 6) -> dict
                  "api": "pagedbatch_b200.engine_hook.install (one sample_tokens launch per step)"},
         "reference": {"decode_steps": steps_ref, "step_ms": 1e3 * med(st_r), "sampling_ms": 1e3 * med(sp_r),
                       "sampling_share": med(sp_r) / med(st_r),
-                      "api": "pagedbatch.sampling.sample_token per row (engine.py:139), CUDA logits"},
+                      "api": "pagedbatch.sampling.sample_token per row (engine.py:139) on the row copied to "
+                             "the host (its CPU request generators cannot drive torch.multinomial on CUDA)"},
         "timing": "host clock around each engine.step() between torch.cuda.synchronize() calls; medians",
     }
     del eng, model

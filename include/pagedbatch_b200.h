@@ -78,10 +78,26 @@ extern "C" {
 typedef struct pb_row_params {
   double temperature; /* 0 => greedy (config.py:156-158); else the row is divided by fp32(temperature) */
   double top_p;       /* (0, 1]; active iff top_p < 1.0 (sampling.py:18) */
-  double uniform;     /* [0, 1) draw for the inverse CDF; ignored for greedy rows */
+  double uniform;     /* rng == 0: the [0, 1) draw for the inverse CDF (ignored for greedy rows);
+                         rng & PB_RNG_PHILOX: the bits of this field are the row's 64-bit seed */
   int32_t top_k;      /* active iff 0 < top_k < vocab (sampling.py:15) */
-  int32_t reserved;   /* must be 0 */
+  uint32_t rng;       /* 0: `uniform` is the draw (drawn on the host, e.g. from the request's
+                         torch.Generator). PB_RNG_PHILOX | step (step < 2^31): the draw is made on
+                         the device, U53 = pb_philox_u53(seed, step), so a request's draws need no
+                         host work and depend only on its seed and its step */
 } pb_row_params;
+
+#define PB_RNG_PHILOX 0x80000000u
+
+/* The device draw of a PB_RNG_PHILOX row, as an integer U53 in [0, 2^53) (the draw is U53 / 2^53):
+ * Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3",
+ * SC 2011) with key (seed low 32 bits, seed high 32 bits) and counter (step, 0, 0, 0); U53 is
+ * (out[0] >> 11) << 32 | out[1]. Host copy of the device function. No counterpart in the
+ * reference, whose draws come from torch.multinomial on the request's generator (sampling.py:27). */
+PB_API uint64_t pb_philox_u53(uint64_t seed, uint32_t step);
+
+/* Philox4x32-10 itself (host copy): ctr[4] and key[2] in, out[4] out. */
+PB_API void pb_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 
 /* What the sampler decided for one row (optional output; used by the parity tests). */
 typedef struct pb_row_info {
@@ -199,6 +215,27 @@ PB_API int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32
  * No counterpart in the reference; a diagnostic for benchmarks and tests. -1 on bad arguments.
  */
 PB_API int pb_sample_launches(int64_t n_rows, int64_t vocab, int dtype, int with_probs);
+
+/*
+ * Finish reasons of the rows just sampled, on the device, right after the sampler on the same
+ * stream (so the engine reads tokens and reasons back together). Replaces the per-row host check
+ * pagedbatch/engine.py:173-182 (LLMEngine._finish_reason), evaluated after the token is appended:
+ *   stop   (1): !ignore_eos and (token == eos_id (eos_id >= 0) or token is one of the row's stop ids)
+ *   length (2): otherwise, output length >= max_tokens, or total length >= max_model_len
+ *   none   (0): otherwise (and for rows whose token is negative: the sampler failed them).
+ *   tokens      device int64[n_rows] (the sampler's out_token)
+ *   row_state   device int32[n_rows][4]: ignore_eos (0/1), output length after the token,
+ *               max_tokens, prompt + output length after the token
+ *   stop_offsets, stop_ids  device CSR of the rows' stop ids: row r's are
+ *               stop_ids[stop_offsets[r] .. stop_offsets[r + 1]); stop_offsets has n_rows + 1 entries
+ *   out_reason  device int8[n_rows]
+ */
+#define PB_FINISH_NONE 0
+#define PB_FINISH_STOP 1
+#define PB_FINISH_LENGTH 2
+PB_API int pb_stop_check(const int64_t* tokens, int64_t n_rows, const int32_t* row_state, const int32_t* stop_offsets,
+                         const int32_t* stop_ids, int32_t eos_id, int32_t max_model_len, int8_t* out_reason,
+                         void* stream);
 
 /* Order-preserving 32-bit key of a float (NaN above +inf, -0 == +0); host helper for tests. */
 PB_API uint32_t pb_key_of(float x);

@@ -24,8 +24,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libpb_oracle.so")
 
 ROW_PARAMS = np.dtype(
-    [("temperature", "<f8"), ("top_p", "<f8"), ("uniform", "<f8"), ("top_k", "<i4"), ("reserved", "<i4")]
+    [("temperature", "<f8"), ("top_p", "<f8"), ("uniform", "<f8"), ("top_k", "<i4"), ("rng", "<u4")]
 )
+RNG_PHILOX = 0x80000000
 ROW_INFO = np.dtype(
     [
         ("thr_key", "<u4"),
@@ -68,6 +69,10 @@ def lib() -> ctypes.CDLL:
         L.pbo_key.restype = ctypes.c_uint32
         L.pbo_key_value.argtypes = [ctypes.c_uint32]
         L.pbo_key_value.restype = ctypes.c_float
+        L.pbo_philox4x32_10.argtypes = [vp, vp, vp]
+        L.pbo_philox4x32_10.restype = None
+        L.pbo_row_u53.argtypes = [vp, vp]
+        L.pbo_row_u53.restype = i32
         _lib = L
     return _lib
 
@@ -91,6 +96,30 @@ def logits_as_numpy(logits) -> tuple[np.ndarray, int]:
     if a.dtype == np.float16:
         return a.view(np.uint16), 2
     return a.astype(np.float32, copy=False), 0
+
+
+def philox4x32_10(ctr, key) -> list[int]:
+    """The oracle's Philox4x32-10 (four counter words, two key words) -> four output words."""
+    c = np.asarray(ctr, dtype=np.uint32)
+    k = np.asarray(key, dtype=np.uint32)
+    o = np.zeros(4, dtype=np.uint32)
+    lib().pbo_philox4x32_10(_ptr(c), _ptr(k), _ptr(o))
+    return [int(v) for v in o]
+
+
+def row_u53(rec: np.ndarray) -> int | None:
+    """The oracle's U53 of one pb_row_params record (None: an unusable host uniform)."""
+    r = np.ascontiguousarray(np.asarray(rec, dtype=ROW_PARAMS).reshape(1))
+    u = np.zeros(1, dtype=np.uint64)
+    return int(u[0]) if lib().pbo_row_u53(_ptr(r), _ptr(u)) else None
+
+
+def make_device_rng_params(temperature, top_p, top_k, seeds, steps) -> np.ndarray:
+    """Records whose draws are made on the device: Philox keyed by each row's 64-bit seed, at `step`."""
+    p = make_params(temperature, top_p, top_k, np.zeros(len(temperature)))
+    p["uniform"] = np.asarray(seeds, dtype=np.uint64).view(np.float64)
+    p["rng"] = RNG_PHILOX | np.asarray(steps, dtype=np.uint32)
+    return p
 
 
 def make_params(temperature, top_p, top_k, uniform) -> np.ndarray:

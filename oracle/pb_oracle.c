@@ -113,6 +113,43 @@ static int load_row(const void* logits, int dtype, int64_t row, int64_t V, int64
 
 /* sort order: key descending, index ascending */
 typedef struct { uint32_t k; uint32_t i; } ent_t;
+
+/* Philox4x32-10 as published (Salmon, Moraes, Dror, Shaw, SC 2011): per round the counter words
+ * (c0, c1, c2, c3) become (hi(M1*c2) ^ c1 ^ k0, lo(M1*c2), hi(M0*c0) ^ c3 ^ k1, lo(M0*c0)) with
+ * M0 = 0xD2511F53 and M1 = 0xCD9E8D57; the key is bumped by (0x9E3779B9, 0xBB67AE85) before every
+ * round but the first. Checked against the algorithm's published known-answer vectors. */
+void pbo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+  uint32_t x[4] = {ctr[0], ctr[1], ctr[2], ctr[3]};
+  uint32_t k[2] = {key[0], key[1]};
+  for (int round = 0; round < 10; round++) {
+    if (round) { k[0] += 0x9E3779B9u; k[1] += 0xBB67AE85u; }
+    uint64_t a = (uint64_t)0xD2511F53u * x[0];
+    uint64_t b = (uint64_t)0xCD9E8D57u * x[2];
+    uint32_t y0 = (uint32_t)(b >> 32) ^ x[1] ^ k[0];
+    uint32_t y2 = (uint32_t)(a >> 32) ^ x[3] ^ k[1];
+    x[0] = y0; x[1] = (uint32_t)b; x[2] = y2; x[3] = (uint32_t)a;
+  }
+  memcpy(out, x, sizeof x);
+}
+
+/* The row's draw as U53 (pagedbatch_b200.h, pb_row_params.rng): the host uniform * 2^53, or for
+ * PB_RNG_PHILOX rows Philox with key = the 64-bit seed stored in `uniform`'s bits and counter
+ * (step, 0, 0, 0), U53 = (out[0] >> 11) << 32 | out[1]. Returns 0 when a host uniform is outside
+ * [0, 1). */
+int pbo_row_u53(const pb_row_params* prm, uint64_t* u53) {
+  if (prm->rng & PB_RNG_PHILOX) {
+    uint64_t seed;
+    memcpy(&seed, &prm->uniform, 8);
+    uint32_t ctr[4] = {prm->rng & 0x7FFFFFFFu, 0, 0, 0}, key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)}, o[4];
+    pbo_philox4x32_10(ctr, key, o);
+    *u53 = ((uint64_t)(o[0] >> 11) << 32) | o[1];
+    return 1;
+  }
+  const double u = prm->uniform;
+  if (!(u >= 0.0 && u < 1.0)) return 0;
+  *u53 = (uint64_t)(u * 0x1p53);
+  return 1;
+}
 static int ent_cmp(const void* a, const void* b) {
   const ent_t* x = (const ent_t*)a; const ent_t* y = (const ent_t*)b;
   if (x->k != y->k) return x->k > y->k ? -1 : 1;
@@ -166,8 +203,8 @@ static void sample_row(const float* x, int64_t V, const pb_row_params* prm, ent_
     if (info) *info = inf;
     return;
   }
-  const double u = prm->uniform;
-  if (!(u >= 0.0 && u < 1.0)) {
+  uint64_t u53;
+  if (!pbo_row_u53(prm, &u53)) {
     inf.status = PB_ROW_BAD_UNIFORM; *tok = -1;
     if (info) *info = inf;
     return;
@@ -199,7 +236,6 @@ static void sample_row(const float* x, int64_t V, const pb_row_params* prm, ent_
   }
 
   /* draw: inverse CDF over the kept prefix (replaces torch.multinomial, sampling.py:27) */
-  uint64_t u53 = (uint64_t)(u * 0x1p53);
   uint64_t t = (uint64_t)(((unsigned __int128)u53 * kept) >> 53);
   uint64_t run = 0;
   int64_t pick = last;

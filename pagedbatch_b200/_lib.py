@@ -23,12 +23,14 @@ ROW_OK, ROW_NONFINITE, ROW_BAD_UNIFORM, ROW_TIMEOUT, ROW_INTERNAL, ROW_BAD_PARAM
 ROW_FALLBACK = 32
 CAND_FALLBACK, CAND_GREEDY, CAND_MAX_CAP = 0x100, 0x200, 2048
 PATH_GREEDY, PATH_SMALL, PATH_LARGE, PATH_STREAM = 1, 2, 4, 8
+FINISH_NONE, FINISH_STOP, FINISH_LENGTH = 0, 1, 2
 MAX_VOCAB = 1 << 24
 
 # struct pb_row_params / pb_row_info (include/pagedbatch_b200.h)
 ROW_PARAMS = np.dtype(
-    [("temperature", "<f8"), ("top_p", "<f8"), ("uniform", "<f8"), ("top_k", "<i4"), ("reserved", "<i4")]
+    [("temperature", "<f8"), ("top_p", "<f8"), ("uniform", "<f8"), ("top_k", "<i4"), ("rng", "<u4")]
 )
+RNG_PHILOX = 0x80000000  # pb_row_params.rng: the draw is made on the device (Philox, seed and step)
 ROW_INFO = np.dtype(
     [
         ("thr_key", "<u4"),
@@ -62,6 +64,9 @@ EXPORTS = (
     "pb_sample_launches",
     "pb_key_of",
     "pb_exp",
+    "pb_philox_u53",
+    "pb_stop_check",
+    "pb_philox4x32_10",
     "pb_strerror",
     "pb_version",
 )
@@ -111,6 +116,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     L.pb_key_of.restype = ctypes.c_uint32
     L.pb_exp.argtypes = [ctypes.c_float]
     L.pb_exp.restype = ctypes.c_float
+    L.pb_stop_check.argtypes = [vp, i64, vp, vp, vp, i32, i32, vp, vp]
+    L.pb_stop_check.restype = i32
+    L.pb_philox_u53.argtypes = [ctypes.c_uint64, ctypes.c_uint32]
+    L.pb_philox_u53.restype = ctypes.c_uint64
+    L.pb_philox4x32_10.argtypes = [vp, vp, vp]
+    L.pb_philox4x32_10.restype = None
     L.pb_strerror.argtypes = [i32]
     L.pb_strerror.restype = ctypes.c_char_p
     L.pb_version.argtypes = []

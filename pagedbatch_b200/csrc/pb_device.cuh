@@ -4,6 +4,9 @@
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
+
+#include "pagedbatch_b200.h"
 
 namespace pb {
 
@@ -83,6 +86,57 @@ __device__ __forceinline__ uint64_t compose(uint32_t key, uint32_t idx) {
 }
 __device__ __forceinline__ uint32_t comp_key(uint64_t c) { return (uint32_t)(c >> 32); }
 __device__ __forceinline__ uint32_t comp_idx(uint64_t c) { return 0xFFFFFFFFu - (uint32_t)c; }
+
+// ---- per-row draws ---------------------------------------------------------------------------
+
+// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3",
+// SC 2011): ten rounds of two 32x32->64 multiplications on a 4-word counter, with a 2-word key
+// bumped by the Weyl constants between rounds.
+__host__ __device__ __forceinline__ void philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2],
+                                                       uint32_t out[4]) {
+  uint32_t c0 = ctr_in[0], c1 = ctr_in[1], c2 = ctr_in[2], c3 = ctr_in[3];
+  uint32_t k0 = key_in[0], k1 = key_in[1];
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0, hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lo1;
+    c2 = n2;
+    c3 = lo0;
+  }
+  out[0] = c0;
+  out[1] = c1;
+  out[2] = c2;
+  out[3] = c3;
+}
+
+// U53 of a PB_RNG_PHILOX row: key = the 64-bit seed, counter = (step, 0, 0, 0).
+__host__ __device__ __forceinline__ uint64_t philox_u53(uint64_t seed, uint32_t step) {
+  const uint32_t ctr[4] = {step, 0u, 0u, 0u}, key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  uint32_t o[4];
+  philox4x32_10(ctr, key, o);
+  return ((uint64_t)(o[0] >> 11) << 32) | o[1];
+}
+
+// A row's draw as U53 (the draw is U53 / 2^53): its host-drawn uniform, or the device draw.
+__host__ __device__ __forceinline__ uint64_t row_u53(const pb_row_params& p) {
+  if (p.rng & PB_RNG_PHILOX) {
+    uint64_t seed;
+    memcpy(&seed, &p.uniform, 8);
+    return philox_u53(seed, p.rng & 0x7FFFFFFFu);
+  }
+  return (uint64_t)(p.uniform * 0x1p53);
+}
+
+// Whether a row's draw is usable: device draws always are; a host draw must lie in [0, 1).
+__host__ __device__ __forceinline__ bool row_draw_ok(const pb_row_params& p) {
+  return (p.rng & PB_RNG_PHILOX) || (p.uniform >= 0.0 && p.uniform < 1.0);
+}
 
 // ---- mbarrier + bulk copy (TMA engine, 1-D, no multicast) -------------------------------
 

@@ -117,7 +117,9 @@ struct Shared {
   int32_t cp_flags[3];             // checkpoint flags (timeout 4, overflow 2, crowded 1)
   uint32_t cp_count[3];            // checkpoint: candidates held by the CTA
   // row parameters
-  double temperature, top_p, uniform;
+  double temperature, top_p;
+  uint64_t u53;      // the row's draw as U53 (host uniform or device draw)
+  int32_t draw_ok;   // the draw is usable
   int32_t top_k, greedy, filtering, status;
   float tf;
   int64_t row;
@@ -1015,7 +1017,8 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     const pb_row_params p = a.params[item];
     sh.temperature = p.temperature;
     sh.top_p = p.top_p;
-    sh.uniform = p.uniform;
+    sh.u53 = row_u53(p);
+    sh.draw_ok = row_draw_ok(p) ? 1 : 0;
     sh.top_k = p.top_k;
     sh.greedy = (p.temperature == 0.0);
     sh.tf = (float)p.temperature;
@@ -1418,14 +1421,14 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
     // a shard whose values are all -inf cannot tell whether the whole row is: it defers
     if (!(a.cand_out && mk <= KEY_NEG_INF)) info.status = PB_ROW_NONFINITE;
     finished = true;
-  } else if (!(sh.uniform >= 0.0 && sh.uniform < 1.0)) {
+  } else if (!sh.draw_ok) {
     info.status = PB_ROW_BAD_UNIFORM;
     finished = true;
   }
 
   const bool topp_active = sh.top_p < 1.0 && (float)sh.top_p < 1.0f;
   const float pf = (float)sh.top_p;
-  const uint64_t u53 = (uint64_t)(sh.uniform * 0x1p53);
+  const uint64_t u53 = sh.u53;
 
   // ---------------- small path: survivors resolved in rank 0 ----------------
   if (!finished && filtering && !sh.any_overflow) {
@@ -2032,7 +2035,8 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
     const pb_row_params p = a.params[item];
     sh.temperature = p.temperature;
     sh.top_p = p.top_p;
-    sh.uniform = p.uniform;
+    sh.u53 = row_u53(p);
+    sh.draw_ok = row_draw_ok(p) ? 1 : 0;
     sh.top_k = p.top_k;
     sh.greedy = (p.temperature == 0.0);
     sh.tf = (float)p.temperature;
@@ -2058,7 +2062,7 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
     else if (bad) sh.status = PB_ROW_BAD_PARAMS;
     else if (sh.greedy) mode = 1;
     else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) sh.status = PB_ROW_NONFINITE;
-    else if (!(p.uniform >= 0.0 && p.uniform < 1.0)) sh.status = PB_ROW_BAD_UNIFORM;
+    else if (!row_draw_ok(p)) sh.status = PB_ROW_BAD_UNIFORM;
     else if ((fl & (PB_CAND_FALLBACK | 0xFF)) || total > MERGE_CAP || total == 0) sh.status = PB_ROW_FALLBACK;
     else mode = 2;
     if (mode == 1 && (fl & ~PB_CAND_GREEDY)) {  // a shard could not publish its maximum
@@ -2123,7 +2127,7 @@ __global__ void __launch_bounds__(NT, 1) merge_kernel(MergeArgs a) {
     const int nk = sh.nk;
     if (nk <= KCAP) {
       const bool topp_active = sh.top_p < 1.0 && (float)sh.top_p < 1.0f;
-      finish_survivors(K, nk, m, topp_active, (float)sh.top_p, (uint64_t)(sh.uniform * 0x1p53), sh, &token, &info);
+      finish_survivors(K, nk, m, topp_active, (float)sh.top_p, sh.u53, sh, &token, &info);
     } else if (tid == 0) {
       info.status = PB_ROW_FALLBACK;
     }
@@ -2202,7 +2206,7 @@ __global__ void __launch_bounds__(MW_ROWS * 32) merge_warp_kernel(MergeArgs m) {
   else if (bad) status = PB_ROW_BAD_PARAMS;
   else if (p.temperature == 0.0) mode = 1;
   else if (mk >= KEY_POS_INF || mk <= KEY_NEG_INF) status = PB_ROW_NONFINITE;
-  else if (!(p.uniform >= 0.0 && p.uniform < 1.0)) status = PB_ROW_BAD_UNIFORM;
+  else if (!row_draw_ok(p)) status = PB_ROW_BAD_UNIFORM;
   else if ((fl & (PB_CAND_FALLBACK | 0xFF)) || total > MERGE_CAP || total == 0) status = PB_ROW_FALLBACK;
   else mode = 2;
   if (mode == 1 && (fl & ~PB_CAND_GREEDY)) {  // a shard could not publish its maximum
@@ -2300,6 +2304,29 @@ __global__ void __launch_bounds__(MW_ROWS * 32) merge_warp_kernel(MergeArgs m) {
     m.out_token[item] = (info.status == PB_ROW_OK) ? token : -1;
     if (m.out_info) m.out_info[item] = info;
   }
+}
+
+// ---- finish reasons (pb_stop_check) ------------------------------------------------------------
+
+// One thread per row: pagedbatch/engine.py:173-182 (_finish_reason) on the token just sampled.
+__global__ void __launch_bounds__(256) stop_check_kernel(const int64_t* tokens, int64_t n_rows, const int4* state,
+                                                         const int32_t* offs, const int32_t* ids, int32_t eos,
+                                                         int32_t max_model_len, int8_t* out) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n_rows) return;
+  const int64_t tok = tokens[r];
+  const int4 st = state[r];  // ignore_eos, output length, max_tokens, total length
+  int8_t reason = PB_FINISH_NONE;
+  if (tok >= 0) {
+    bool stop = false;
+    if (!st.x) {
+      stop = eos >= 0 && tok == eos;
+      for (int32_t i = offs[r]; !stop && i < offs[r + 1]; ++i) stop = tok == ids[i];
+    }
+    if (stop) reason = PB_FINISH_STOP;
+    else if (st.y >= st.z || st.w >= max_model_len) reason = PB_FINISH_LENGTH;
+  }
+  out[r] = reason;
 }
 
 // Per-device one-time set-up (a function attribute, a device property): a bit per device, set
@@ -2734,6 +2761,23 @@ uint32_t pb_key_of(float x) {
   }
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
+
+int pb_stop_check(const int64_t* tokens, int64_t n_rows, const int32_t* row_state, const int32_t* stop_offsets,
+                  const int32_t* stop_ids, int32_t eos_id, int32_t max_model_len, int8_t* out_reason, void* stream) {
+  if (n_rows < 0) return PB_E_INVALID;
+  if (n_rows == 0) return PB_OK;
+  if (!tokens || !row_state || !stop_offsets || !out_reason) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(row_state) & 15) != 0) return PB_E_INVALID;
+  if (n_rows > (int64_t)0x7FFFFFFF * 256) return PB_E_INVALID;
+  stop_check_kernel<<<(unsigned)((n_rows + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      tokens, n_rows, reinterpret_cast<const int4*>(row_state), stop_offsets, stop_ids, eos_id, max_model_len,
+      out_reason);
+  return cudaGetLastError() == cudaSuccess ? PB_OK : PB_E_LAUNCH;
+}
+
+uint64_t pb_philox_u53(uint64_t seed, uint32_t step) { return philox_u53(seed, step); }
+
+void pb_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) { philox4x32_10(ctr, key, out); }
 
 float pb_exp(float d) {
   // host copy of exp_weight: same operation sequence

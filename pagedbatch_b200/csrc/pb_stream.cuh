@@ -68,7 +68,7 @@ __device__ __forceinline__ int fast_mode(const pb_row_params& p, int64_t V) {
   const bool bad = !(p.temperature >= 0.0) || !(p.top_p > 0.0 && p.top_p <= 1.0) || p.top_k < 0;
   if (bad) return F_NONE;
   if (p.temperature == 0.0) return F_GREEDY;
-  if (p.top_k > 0 && p.top_k <= F_KMAX && (int64_t)p.top_k < V && p.uniform >= 0.0 && p.uniform < 1.0)
+  if (p.top_k > 0 && p.top_k <= F_KMAX && (int64_t)p.top_k < V && row_draw_ok(p))
     return F_FILTER;
   return F_NONE;
 }
@@ -493,7 +493,7 @@ __device__ void finish_list(const FastArgs& a, const pb_row_params& p, int64_t i
   }
   const bool topp = p.top_p < 1.0 && (float)p.top_p < 1.0f;
   Finish f;
-  warp_finish_sorted<NPL>(v, S, m, topp, (float)p.top_p, (uint64_t)(p.uniform * 0x1p53), &f);
+  warp_finish_sorted<NPL>(v, S, m, topp, (float)p.top_p, row_u53(p), &f);
   if (lane == 0) {
     a.out_token[item] = f.ok ? f.token : -1;
     if (a.out_info) {

@@ -24,8 +24,11 @@ from . import _lib
 _DTYPE_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 
-def pack_params(temperature, top_p, top_k, uniform) -> np.ndarray:
-    """Per-row parameter records (struct pb_row_params) as a numpy structured array."""
+def pack_params(temperature, top_p, top_k, uniform, seeds=None, steps=None) -> np.ndarray:
+    """Per-row parameter records (struct pb_row_params) as a numpy structured array.
+
+    With ``seeds`` and ``steps`` the rows' draws are made on the device (Philox keyed by the
+    64-bit seed at that step, ``PB_RNG_PHILOX``) and ``uniform`` is ignored."""
     n = len(temperature)
     rec = np.zeros(n, dtype=_lib.ROW_PARAMS)
     rec["temperature"] = temperature
@@ -33,7 +36,14 @@ def pack_params(temperature, top_p, top_k, uniform) -> np.ndarray:
     # any top_k at or above the vocabulary switches the filter off (sampling.py:15), so values past
     # the int32 field saturate instead of failing
     rec["top_k"] = np.minimum(np.asarray(top_k, dtype=np.int64), np.iinfo(np.int32).max)
-    rec["uniform"] = uniform
+    if seeds is None:
+        rec["uniform"] = uniform
+    else:
+        st = np.asarray(steps, dtype=np.int64)
+        if st.shape != (n,) or (n and (st.min() < 0 or st.max() >= 1 << 31)):
+            raise ValueError("steps must hold one value in [0, 2^31) per row")
+        rec["uniform"] = (np.asarray(seeds, dtype=np.int64).astype(np.uint64)).view(np.float64)
+        rec["rng"] = _lib.RNG_PHILOX | st.astype(np.uint32)
     return rec
 
 

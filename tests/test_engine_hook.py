@@ -28,16 +28,32 @@ def _stand_in_row(logits, params, generator):
     return min(int(u * x.numel()), x.numel() - 1)
 
 
-def _stand_in_batch(logits, params, generators, rows=None):
+def _stand_in_launch(logits, params, generators, rows=None, *, steps=None, seeds=None):
     rows = range(logits.shape[0]) if rows is None else rows
-    return [_stand_in_row(logits[r], p, g) for r, p, g in zip(rows, params, generators, strict=True)]
+    toks = [_stand_in_row(logits[r], p, g) for r, p, g in zip(rows, params, generators, strict=True)]
+    return torch.tensor(toks, dtype=torch.int64), logits, None, None
+
+
+def _stand_in_stop(tokens, ignore_eos, out_lens, max_tokens, total_lens, stop_ids, eos, max_model_len):
+    """The finish rule of pagedbatch/engine.py:173-182 per row (0 none, 1 stop, 2 length)."""
+    out = []
+    for t, ig, ol, mt, tl, st in zip(tokens.tolist(), ignore_eos, out_lens, max_tokens, total_lens, stop_ids,
+                                     strict=True):
+        if not ig and ((eos is not None and t == eos) or t in st):
+            out.append(1)
+        elif ol >= mt or tl >= max_model_len:
+            out.append(2)
+        else:
+            out.append(0)
+    return torch.tensor(out, dtype=torch.int8)
 
 
 @pytest.fixture
 def stand_in(monkeypatch):
     from pagedbatch_b200 import engine_hook
 
-    monkeypatch.setattr(engine_hook, "sample_tokens", _stand_in_batch)
+    monkeypatch.setattr(engine_hook, "launch_rows", _stand_in_launch)
+    monkeypatch.setattr(engine_hook, "stop_reasons", _stand_in_stop)
     monkeypatch.setattr(engine_hook, "_sample_one", _stand_in_row)
     yield engine_hook
     engine_hook.restore_module(ref[1])
@@ -87,3 +103,41 @@ def test_dispatcher_refuses_extra_tokens(stand_in):
             hook.dispatch_sample_token(None, None, None)
     finally:
         hook._LOCAL.tokens = None
+
+
+def test_finish_reasons_and_histogram(stand_in):
+    """Finish reasons served from the (stand-in) device check equal the engine's own: requests that
+    stop on a stop id or EOS, and ones that hit max_tokens; the sampling histogram is rendered."""
+    from pagedbatch.config import SamplingParams
+
+    hook = stand_in
+    reqs = [([5, 6, 7], SamplingParams(temperature=0.0, max_tokens=4)),
+            ([9, 9], SamplingParams(temperature=0.0, max_tokens=50, stop_token_ids=tuple(range(258)))),
+            ([1, 2, 3, 4], SamplingParams(temperature=0.9, max_tokens=6, seed=3, stop_token_ids=(11, 12))),
+            ([3], SamplingParams(temperature=0.0, max_tokens=7, ignore_eos=True))]
+
+    def finals(eng):
+        for i, (p, sp) in enumerate(reqs):
+            eng.add_request(prompt_token_ids=p, sampling=sp, request_id=f"q{i}")
+        out = {}
+        while eng.has_unfinished_requests:
+            for o in eng.step():
+                if o.finished:
+                    out[o.request_id] = (o.finish_reason, list(o.output_token_ids))
+        return out
+
+    em = ref[1]
+    saved = em.sample_token
+    em.sample_token = _stand_in_row  # the same per-row sampler, with the engine's own finish check
+    try:
+        plain = finals(R.build_tiny_engine("cpu"))
+    finally:
+        em.sample_token = saved
+    eng = R.build_tiny_engine("cpu")
+    hook.install(eng)
+    batched = finals(eng)
+    assert batched == plain
+    assert batched["q1"][0] == "stop" and batched["q0"][0] == "length"
+    text = eng.metrics.render()
+    assert "pagedbatch_sampling_seconds_count" in text and "pagedbatch_step_seconds_count" in text
+    assert eng.metrics.sampling_seconds.count > 0
