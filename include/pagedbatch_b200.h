@@ -132,15 +132,16 @@ PB_API int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t voca
                      pb_row_info* out_info, float* out_probs, void* stream);
 
 /*
- * The same sampler as stream-ordered launches over a caller-provided workspace: a memset of the
- * workspace's per-row counters, a persistent pass (one wave of CTAs walking fixed-size pieces of
- * the rows; greedy rows and top-k rows with k <= 256; each row merged from its pieces' candidate
- * records by the CTA that finishes its last piece), and pb_sample's full-row kernel restricted to
- * the rows the pass could not settle. Results are identical to pb_sample. Replaces the same call as
- * pb_sample (pagedbatch/sampling.py:10-27). With out_probs, or for a vocabulary too long to cut
- * into at most 64 pieces, it runs pb_sample itself. workspace: device memory of at least
- * pb_sample_ws_bytes(n_rows, vocab, dtype) bytes, 256-byte aligned, not used by another call while
- * this one runs.
+ * The same sampler as stream-ordered launches over a caller-provided workspace: the persistent
+ * streaming kernel in balanced mode (the batch cut into equal shares of 16-byte vectors, one per
+ * SM, so a row may be split between neighbouring CTAs; each piece of a split row publishes a record
+ * in the workspace and the piece that arrives last, counted on a per-row counter in the workspace,
+ * merges the row), then pb_sample's cluster kernel restricted to the rows the streaming kernel does
+ * not take or could not settle. Results are identical to pb_sample. Replaces the same call as
+ * pb_sample (pagedbatch/sampling.py:10-27). With out_probs it runs pb_sample itself. workspace:
+ * device memory of at least pb_sample_ws_bytes(n_rows, vocab, dtype) bytes, 256-byte aligned, of
+ * any content (the counters carry a check word and every record is written before it is read), not
+ * used by another call while this one runs.
  */
 PB_API int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype);
 PB_API int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
@@ -154,11 +155,11 @@ PB_API int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t v
  * fixed scratch array compiled into the library instead of a workspace. Every GPU that loads the
  * library holds that array (pb_sample_noalloc_max_bytes(), 32 MiB) until the process exits.
  * Same arguments and results as pb_sample_ws without out_probs (probabilities need pb_sample).
- * A batch that needs more scratch than the array holds (about 1000 rows of 128256 fp32 logits,
- * about 7900 rows of 49152 bf16 logits; pb_sample_ws_bytes gives the need) returns PB_E_SCRATCH
- * and launches nothing. The first call on each device looks up the array's device address; make that call
- * before any stream capture. All calls share the one array, so calls that overlap on the GPU
- * (two streams, or two host threads) race and corrupt each other's results; keep them ordered.
+ * A batch that needs more scratch than the array holds (about 1000 rows of 128256 fp32 logits;
+ * pb_sample_ws_bytes gives the need) returns PB_E_SCRATCH and launches nothing. The first call on
+ * each device looks up the array's device address; make that call before any stream capture. All
+ * calls share the one array, so calls that overlap on the GPU (two streams, or two host threads)
+ * race and corrupt each other's results; keep them ordered.
  */
 PB_API int64_t pb_sample_noalloc_max_bytes(void);
 PB_API int pb_sample_noalloc(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,

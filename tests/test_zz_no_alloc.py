@@ -77,10 +77,11 @@ def test_noalloc_refuses_a_batch_larger_than_its_scratch(cuda):
 
 
 def test_noalloc_without_info_keeps_row_state_in_its_array(cuda):
-    """Without out_info the per-row results between the pass and the full-row launch live in the
-    fixed array itself. Two calls in a row, the second on a different batch whose rows must reach
-    the full-row launch (a greedy row with a NaN, top_k above what the pass settles, temperature-only
-    and top-p-only rows), so that it reads only what it wrote, never the first call's leftovers."""
+    """Without out_info, what the streaming launch leaves for the cluster kernel that follows lives
+    in the fixed array and the tokens themselves. Two calls in a row, the second on a different
+    batch whose rows must reach the cluster kernel (a greedy row with a NaN, top_k above what the
+    streaming kernel settles, temperature-only and top-p-only rows), so that it reads only what it
+    wrote, never the first call's leftovers."""
     w = workloads.config2(rows=40)
     x = w.logits.to(cuda)
     rec = oracle.make_params([p.temperature for p in w.params], [p.top_p for p in w.params],
