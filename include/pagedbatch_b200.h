@@ -132,21 +132,31 @@ PB_API int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t voca
                      pb_row_info* out_info, float* out_probs, void* stream);
 
 /*
- * The same sampler as stream-ordered launches over a caller-provided workspace: the persistent
+ * The same sampler as stream-ordered launches over a caller-provided workspace. Results are
+ * identical to pb_sample. Replaces the same call as pb_sample (pagedbatch/sampling.py:10-27).
+ * When every row starts on a 16-byte boundary (logits and row_stride * element size multiples of
+ * 16), three launches:
+ *   1. a streaming pass that reads the batch once and writes, per row, the key of the largest value
+ *      of each 128-byte group (1/32 of the logits' bytes, in the workspace);
+ *   2. one CTA per row that settles greedy rows and rows with 0 < top_k <= 128 from the groups that
+ *      can hold their survivors (re-reading only those);
+ *   3. pb_sample's cluster kernel over the other rows and the ones pass 2 could not settle.
+ * Otherwise (or with the environment variable PB_WS=balanced), two launches: the persistent
  * streaming kernel in balanced mode (the batch cut into equal shares of 16-byte vectors, one per
  * SM, so a row may be split between neighbouring CTAs; each piece of a split row publishes a record
  * in the workspace and the piece that arrives last, counted on a per-row counter in the workspace,
- * merges the row), then pb_sample's cluster kernel restricted to the rows the streaming kernel does
- * not take or could not settle. Results are identical to pb_sample. Replaces the same call as
- * pb_sample (pagedbatch/sampling.py:10-27). With out_probs it runs pb_sample itself. workspace:
- * device memory of at least pb_sample_ws_bytes(n_rows, vocab, dtype) bytes, 256-byte aligned, of
- * any content (the counters carry a check word and every record is written before it is read), not
- * used by another call while this one runs.
+ * merges the row), then the cluster kernel over the rows it does not take or could not settle.
+ * With out_probs it runs pb_sample itself. workspace: device memory of at least
+ * pb_sample_ws_bytes(n_rows, vocab, dtype) bytes (enough for either launch), 256-byte aligned, of
+ * any content (every group key and record is written before it is read; the counters carry a check
+ * word), not used by another call while this one runs. pb_sample_ws_launches gives the number of
+ * launches for a batch (a diagnostic for benchmarks; no counterpart in the reference).
  */
 PB_API int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype);
 PB_API int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
                         const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
                         pb_row_info* out_info, float* out_probs, void* workspace, int64_t ws_bytes, void* stream);
+PB_API int pb_sample_ws_launches(const void* logits, int64_t n_rows, int64_t vocab, int64_t row_stride, int dtype);
 
 /*
  * pb_sample_ws for callers that cannot allocate device memory: no counterpart in the reference.
@@ -155,8 +165,9 @@ PB_API int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t v
  * fixed scratch array compiled into the library instead of a workspace. Every GPU that loads the
  * library holds that array (pb_sample_noalloc_max_bytes(), 32 MiB) until the process exits.
  * Same arguments and results as pb_sample_ws without out_probs (probabilities need pb_sample).
- * A batch that needs more scratch than the array holds (about 1000 rows of 128256 fp32 logits;
- * pb_sample_ws_bytes gives the need) returns PB_E_SCRATCH and launches nothing. The first call on
+ * It takes the three-launch form of pb_sample_ws while its group keys fit the array (up to 2092
+ * rows of 128256 fp32 logits, 4185 of bf16) and the balanced form beyond; a batch too large for
+ * both returns PB_E_SCRATCH and launches nothing. The first call on
  * each device looks up the array's device address; make that call before any stream capture. All
  * calls share the one array, so calls that overlap on the GPU (two streams, or two host threads)
  * race and corrupt each other's results; keep them ordered.

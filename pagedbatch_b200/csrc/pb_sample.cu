@@ -972,6 +972,7 @@ __device__ void finish_survivors(uint64_t* K, int nk, float m, bool topp_active,
 }
 
 #include "pb_stream.cuh"
+#include "pb_groups.cuh"
 
 template <typename T>
 __global__ void __launch_bounds__(NT, 2) sample_kernel(Args a) {
@@ -2533,6 +2534,113 @@ int run_ws(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab,
   return run_balanced<__half>(a, workspace, grid, es, st);
 }
 
+// ---- two-pass workspace path (pb_groups.cuh) ---------------------------------------------------
+
+// Its geometry for a batch: group keys per row (and their row stride), pass-1 tasks, pass-2
+// coarsening, workspace bytes.
+struct GroupPlan {
+  int64_t ngr, ngs, ntasks, coarse, bytes;
+};
+
+GroupPlan group_plan(int64_t n_rows, int64_t vocab, int es) {
+  GroupPlan g;
+  const int64_t ge = GM_GB / es;
+  g.ngr = (vocab + ge - 1) / ge;
+  g.ngs = (g.ngr + 3) & ~(int64_t)3;
+  g.ntasks = (n_rows * g.ngr + 3) / 4;
+  g.coarse = (g.ngr + GS_MAXG - 1) / GS_MAXG;
+  g.bytes = align256(n_rows * g.ngs * 4);
+  return g;
+}
+
+// Rows the two-pass path can read: every row starts on a 16-byte boundary (its passes load whole
+// 16-byte vectors from a row's start) and the batch has fewer than 2^31 groups. PB_WS=balanced
+// selects the balanced streaming launch instead.
+bool groups_eligible(const void* logits, int64_t row_stride, int es, int64_t n_rows, int64_t vocab) {
+  const char* env = getenv("PB_WS");
+  if (env && strcmp(env, "balanced") == 0) return false;
+  if (n_rows * group_plan(1, vocab, es).ngs >= (int64_t)0x7FFFFFFF) return false;
+  return (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && ((row_stride * es) & 15) == 0;
+}
+
+// Pass-1 grid: the CTAs that fit on the device at once (at least one task per warp).
+template <typename T>
+int64_t group_grid(int64_t ntasks) {
+  static DeviceInt occ;
+  int dev = 0;
+  if (current_device(&dev) != PB_OK) dev = 0;
+  int per_sm = occ.v[dev].load(std::memory_order_relaxed);
+  if (!per_sm) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, group_max_kernel<T>, GM_THREADS, 0) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = GM_MINB;
+    occ.v[dev].store(per_sm, std::memory_order_relaxed);
+  }
+  const int64_t full = (int64_t)per_sm * sm_count();
+  return std::max<int64_t>(1, std::min<int64_t>(full, (ntasks + GM_WARPS - 1) / GM_WARPS));
+}
+
+// pass 1 -> pass 2 (programmatic dependency) -> cluster kernel over the rows pass 2 left
+template <typename T>
+int run_groups(const Args& a, uint8_t* workspace, int es, cudaStream_t st) {
+  const GroupPlan gp = group_plan(a.n_rows, a.vocab, es);
+  GroupArgs g;
+  g.logits = a.logits;
+  g.n_rows = a.n_rows;
+  g.vocab = a.vocab;
+  g.row_stride_bytes = a.row_stride * es;
+  g.row_index = a.row_index;
+  g.params = a.params;
+  g.out_token = a.out_token;
+  g.out_info = a.out_info;
+  g.gmax = reinterpret_cast<uint32_t*>(workspace);
+  g.ngr = (int32_t)gp.ngr;
+  g.ngs = (int32_t)gp.ngs;
+  g.coarse = (int32_t)gp.coarse;
+  g.ntasks = gp.ntasks;
+  group_max_kernel<T><<<(unsigned)group_grid<T>(gp.ntasks), GM_THREADS, 0, st>>>(g);
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  const bool pdl = getenv("PB_NO_PDL") == nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.n_rows, 1, 1);
+  cfg.blockDim = dim3(GS_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, group_settle_kernel<T>, g) != cudaSuccess) return PB_E_LAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
+  Args c = a;
+  c.complement = 1;
+  return launch<T>(c, cluster_size_for(a.n_rows, a.vocab, es), st, pdl);
+}
+
+int run_groups_dtype(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                     const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
+                     pb_row_info* out_info, uint8_t* workspace, cudaStream_t st) {
+  Args a;
+  a.logits = static_cast<const char*>(logits);
+  a.n_rows = n_rows;
+  a.vocab = vocab;
+  a.row_stride = row_stride;
+  a.row_index = row_index;
+  a.params = params;
+  a.out_token = out_token;
+  a.out_info = out_info;
+  a.out_probs = nullptr;
+  a.only_fallback = nullptr;
+  a.complement = 0;
+  a.cand_out = nullptr;
+  a.cand_cap = 0;
+  a.vocab_offset = 0;
+  if (dtype == PB_DTYPE_F32) return run_groups<float>(a, workspace, es, st);
+  if (dtype == PB_DTYPE_BF16) return run_groups<__nv_bfloat16>(a, workspace, es, st);
+  return run_groups<__half>(a, workspace, es, st);
+}
+
 // ---- allocation-free entry point -------------------------------------------------------------
 // Some callers cannot allocate device memory at all: plugins whose host application owns every
 // byte of the GPU through its own allocator, or C callers with no allocator of their own. For
@@ -2651,6 +2759,13 @@ int pb_sample(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int6
 
 int64_t pb_record_bytes(int32_t cap) { return record_bytes(cap); }
 
+int pb_sample_ws_launches(const void* logits, int64_t n_rows, int64_t vocab, int64_t row_stride, int dtype) {
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
+  if (n_rows == 0) return 0;
+  return groups_eligible(logits, row_stride, es, n_rows, vocab) ? 3 : 2;
+}
+
 int pb_sample_launches(int64_t n_rows, int64_t vocab, int dtype, int with_probs) {
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
@@ -2703,7 +2818,8 @@ int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap,
 int64_t pb_sample_ws_bytes(int64_t n_rows, int64_t vocab, int dtype) {
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es || n_rows < 0 || vocab <= 0) return PB_E_INVALID;
-  return ws_need(n_rows, (int64_t)F_CPS * sm_count());  // (the grid never exceeds F_CPS CTAs per SM)
+  // either launch: the balanced one (its grid never exceeds F_CPS CTAs per SM) or the two-pass one
+  return std::max(ws_need(n_rows, (int64_t)F_CPS * sm_count()), group_plan(n_rows, vocab, es).bytes);
 }
 
 int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
@@ -2721,6 +2837,9 @@ int pb_sample_ws(const void* logits, int dtype, int64_t n_rows, int64_t vocab, i
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  if (groups_eligible(logits, row_stride, es, n_rows, vocab) && ws_bytes >= group_plan(n_rows, vocab, es).bytes)
+    return run_groups_dtype(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
+                            static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
   const int64_t grid = balanced_grid(n_rows, vocab, es);
   if (ws_bytes < ws_need(n_rows, grid)) return PB_E_INVALID;
   return run_ws(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
@@ -2740,11 +2859,16 @@ int pb_sample_noalloc(const void* logits, int dtype, int64_t n_rows, int64_t voc
   const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
   if (!es) return PB_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  const bool groups = groups_eligible(logits, row_stride, es, n_rows, vocab) &&
+                      group_plan(n_rows, vocab, es).bytes <= NOALLOC_SCRATCH_BYTES;
   const int64_t grid = balanced_grid(n_rows, vocab, es);
-  if (ws_need(n_rows, grid) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
+  if (!groups && ws_need(n_rows, grid) > NOALLOC_SCRATCH_BYTES) return PB_E_SCRATCH;
   uint8_t* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != PB_OK) return rc;
+  if (groups)  // every group key pass 2 reads is written by pass 1 first
+    return run_groups_dtype(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info,
+                            scratch, static_cast<cudaStream_t>(stream));
   // the launches need no cleared memory: the arrival counters carry a check word (see f_arrive) and
   // every record is written before it is read
   return run_ws(logits, dtype, es, n_rows, vocab, row_stride, row_index, params, out_token, out_info, scratch,

@@ -28,26 +28,42 @@ def _check(g_tok, g_info, o_tok, o_info, label):
     assert np.array_equal(g_info["max_key"], o_info["max_key"], equal_nan=True), label
 
 
-def _run_with_path(dev, rec, row_index, path):
-    """Tokens and info through one launch path (PB_PATH as the ops layer and the library read it)."""
-    old = os.environ.get("PB_PATH")
+def _run_with_path(dev, rec, row_index, path, ws=None):
+    """Tokens and info through one launch path (PB_PATH as the ops layer and the library read it;
+    PB_WS=balanced makes pb_sample_ws take its balanced streaming launch)."""
+    saved = {k: os.environ.get(k) for k in ("PB_PATH", "PB_WS")}
     os.environ["PB_PATH"] = path
+    if ws is None:
+        os.environ.pop("PB_WS", None)
+    else:
+        os.environ["PB_WS"] = ws
     try:
         return run_gpu(dev, rec, row_index, False)
     finally:
-        if old is None:
-            os.environ.pop("PB_PATH", None)
-        else:
-            os.environ["PB_PATH"] = old
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
 
 
-def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""):
+def padded(logits_cpu, pad_to, device="cuda"):
+    """The logits on the device with a row stride of pad_to elements (rows padded with NaN)."""
+    B, V = logits_cpu.shape
+    buf = torch.full((B, pad_to), float("nan"), dtype=logits_cpu.dtype, device=device)
+    view = buf[:, :V]
+    view.copy_(logits_cpu)
+    return view
+
+
+def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label="", pad_to=None):
     """GPU against the oracle. With probs: the launch that writes probabilities (the cluster kernel
     alone), then the same rows without probabilities through pb_sample's streaming kernel (whole
-    rows per CTA) and through pb_sample_ws (the balanced streaming launch, rows cut into pieces),
-    each followed by the cluster kernel on the rows it leaves. Without probs: the path PB_PATH
-    selects (pb_sample_ws by default)."""
-    dev = logits_cpu.to(device)
+    rows per CTA) and through both launches of pb_sample_ws (the two passes over 128-byte group
+    keys when rows are 16-byte aligned; the balanced streaming launch, rows cut into pieces), each
+    followed by the cluster kernel on the rows it leaves. Without probs: the path PB_PATH and PB_WS
+    select. pad_to: the rows pass with that stride (in elements)."""
+    dev = logits_cpu.to(device) if pad_to is None else padded(logits_cpu, pad_to, device)
     g_tok, g_info, g_pr = run_gpu(dev, rec, row_index, probs)
     o_tok, o_info, o_pr = oracle.sample(logits_cpu, rec, row_index, want_probs=probs)
     _check(g_tok, g_info, o_tok, o_info, label)
@@ -56,9 +72,9 @@ def compare(logits_cpu, rec, row_index=None, probs=True, device="cuda", label=""
         same = g_pr[ok].view(np.uint32) == o_pr[ok].view(np.uint32)
         rows_bad = np.flatnonzero(~same.all(axis=1))
         assert rows_bad.size == 0, f"{label}: probs differ on rows {rows_bad[:10]}"
-        for path in ("stream", "ws"):
-            s_tok, s_info, _ = _run_with_path(dev, rec, row_index, path)
-            _check(s_tok, s_info, o_tok, o_info, f"{label} ({path} path)")
+        for path, ws in (("stream", None), ("ws", None), ("ws", "balanced")):
+            s_tok, s_info, _ = _run_with_path(dev, rec, row_index, path, ws)
+            _check(s_tok, s_info, o_tok, o_info, f"{label} ({path} path{', ' + ws if ws else ''})")
     return g_tok, g_info
 
 

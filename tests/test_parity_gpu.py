@@ -26,6 +26,7 @@ def _need_cuda(cuda):
     os.environ.pop("PB_CLUSTER", None)
     os.environ.pop("PB_BALANCED_GRID", None)
     os.environ.pop("PB_PATH", None)
+    os.environ.pop("PB_WS", None)
 
 
 def test_golden_rows(golden):
@@ -269,11 +270,27 @@ def test_vocab_parallel_api_one_rank_nccl():
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("grid", ["1", "3", "16", "148"])
-def test_balanced_path_modes_and_edges(grid):
-    """pb_sample_ws (balanced streaming launch + cluster kernel on the rest) against the oracle, with
-    the grid capped so rows are cut into different numbers of pieces."""
+def _ws_kernel(ws):
+    """pb_sample_ws's launch: "groups" (the two passes over group keys; its default for 16-byte
+    aligned rows) or "balanced" (the balanced streaming launch)."""
     os.environ["PB_PATH"] = "ws"
+    if ws == "balanced":
+        os.environ["PB_WS"] = "balanced"
+    else:
+        os.environ.pop("PB_WS", None)
+
+
+WS_KERNELS = ["groups", "balanced"]
+
+
+@pytest.mark.parametrize("ws,grid", [("balanced", "1"), ("balanced", "3"), ("balanced", "16"), ("balanced", "148"),
+                                     ("groups", "148")])
+def test_balanced_path_modes_and_edges(ws, grid):
+    """pb_sample_ws (either launch, then the cluster kernel on the rest) against the oracle; for the
+    balanced launch with the grid capped so rows are cut into different numbers of pieces. Rows
+    whose bytes are not a multiple of 16 take the balanced launch in any case (the two passes read
+    whole 16-byte vectors from each row's start)."""
+    _ws_kernel(ws)
     os.environ["PB_BALANCED_GRID"] = grid
     rng = np.random.default_rng(20 + int(grid))
     for V in (1, 3, 17, 258, 4099, 49152, 128256):
@@ -309,8 +326,9 @@ def test_balanced_path_modes_and_edges(grid):
     compare(torch.randn(4, 100), rec, probs=False, label="balanced bad params")
 
 
-def test_balanced_path_configs_and_row_index():
-    os.environ["PB_PATH"] = "ws"
+@pytest.mark.parametrize("ws", WS_KERNELS)
+def test_balanced_path_configs_and_row_index(ws):
+    _ws_kernel(ws)
     for w in (workloads.config0(), workloads.config1(), workloads.config2(), workloads.config3(rows=300)):
         compare(w.logits, rec_for(w.params, w.uniforms()), probs=False, label=f"balanced {w.name}")
     # many rows per CTA, and rows cut into many pieces
@@ -334,8 +352,44 @@ def test_balanced_path_configs_and_row_index():
     os.environ.pop("PB_PATH")
 
 
-def test_balanced_path_ties_and_sparse_rows():
-    os.environ["PB_PATH"] = "ws"
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_group_passes_padded_rows(dtype):
+    """The two-pass launch on rows padded to a 16-byte stride: vocabularies whose last vector is
+    partial (read element by element), one-group and sub-group rows, rows read as coarse groups
+    (more than 4096 groups), row_index, every mode, and rows with non-finite values; each against
+    the oracle and, through compare's probabilities run, every other path."""
+    _ws_kernel("groups")
+    es = torch.finfo(dtype).bits // 8
+    epv = 16 // es
+    rng = np.random.default_rng(es)
+    for V in (1, 3, 17, 63, 65, 258, 4099, 49155, 128257, (1 << 20) + 5):
+        B = 12 if V < (1 << 20) else 3
+        x = workloads.head_boosted(B, V, seed=V).to(dtype)
+        t = rng.choice([0.0, 0.7, 1.0, 1.5], B)
+        k = rng.choice([0, 1, 2, 20, 50, 128, 129, max(1, V - 1), V], B)
+        p = rng.choice([1.0, 0.9, 0.99, 1e-6], B)
+        pad = (V + epv - 1) // epv * epv + epv
+        compare(x, oracle.make_params(t, p, k, rng.random(B)), probs=(V <= 4099), pad_to=pad,
+                label=f"groups padded {dtype} V={V}")
+    V = 40990
+    x = torch.full((6, V), float("-inf"))
+    for r, n in enumerate((1, 37, 500, 999, 3, 60)):
+        cols = torch.from_numpy(rng.choice(V, n, replace=False))
+        x[r, cols] = torch.randn(n, generator=torch.Generator().manual_seed(r)) * 2.0
+    x[4, 7] = float("nan")
+    x[5, 40989] = float("inf")
+    x = x.to(dtype)
+    rec = oracle.make_params([1.0, 0.7, 1.0, 1.3, 0.0, 1.0], [1.0, 0.9, 1.0, 0.5, 1.0, 1.0], [100, 100, 128, 100, 0, 5],
+                             rng.random(6))
+    compare(x, rec, probs=False, pad_to=V + 2 * epv, label=f"groups sparse-finite {dtype}")
+    sel = np.array([5, 0, 3, 3, 1], np.int32)
+    rec2 = oracle.make_params([0.0, 1.0, 0.7, 0.7, 1.0], [1.0] * 5, [0, 50, 50, 2, 128], rng.random(5))
+    compare(x, rec2, sel, probs=False, pad_to=V + epv, label=f"groups row_index {dtype}")
+
+
+@pytest.mark.parametrize("ws", WS_KERNELS)
+def test_balanced_path_ties_and_sparse_rows(ws):
+    _ws_kernel(ws)
     V = 20000
     x = torch.zeros(6, V)
     x[1, ::3] = 1.0
