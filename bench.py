@@ -268,11 +268,11 @@ def pct(xs, q):
     return float(np.percentile(np.asarray(xs, dtype=np.float64), q)) if xs else None
 
 
-def launches_per_step(L, logits) -> int:
+def launches_per_step(L, logits, params) -> int:
     """Kernel launches of one sample_op on these logits (the path the ops layer takes)."""
     B, V = logits.shape
     code = ops._DTYPE_CODE[logits.dtype]
-    if ops._ws_path():
+    if ops._ws_path(params, V):
         return L.pb_sample_ws_launches(logits.data_ptr(), B, V, logits.stride(0), code)
     return L.pb_sample_launches(B, V, code, 0)
 
@@ -292,7 +292,7 @@ def device_config_measure(w, dev, stream, steps: int):
     out = {"us_per_step": step_ms * 1e3, "rows_per_s": B / (step_ms / 1e3),
            "per_launch_us": {"p50": pct(launches, 50), "p99": pct(launches, 99)},
            "hbm_frac": B * V * elem / (step_ms / 1e3) / 1e9 / peak,
-           "gpu_launches_per_step": launches_per_step(L, bufs[0]),
+           "gpu_launches_per_step": launches_per_step(L, bufs[0], params),
            "clocks": clocks, "config": workload_config(w)}
     del bufs
     torch.cuda.empty_cache()
@@ -620,7 +620,7 @@ def run_ours(args):
     achieved = alg_bytes / (step_ms / 1e3) / 1e9
     # pb_sample_ws (the default path): the balanced streaming kernel, then the cluster kernel over the
     # rows it leaves; pb_sample: 1 or 2 launches by shape
-    per_step_launches = launches_per_step(L, bufs[0])
+    per_step_launches = launches_per_step(L, bufs[0], params)
     line = {
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3, "higher_is_better": True,

@@ -16,11 +16,12 @@
 //
 // Pass 2 (group_settle_kernel), one CTA per row, after pass 1 (programmatic launch dependency):
 //   greedy rows: the first group holding the row's largest key is re-read for its first maximum.
-//   top-k rows (k <= F_KMAX): each of the 8 warps takes the ceil(k / 8)-th largest of its group
-//     keys; the smallest of these, b, is reached by at least k group keys, so by at least k values:
+//   top-k rows (k <= F_KMAX): each of the 8 warps takes the ceil(k / 8)-th largest of its lanes'
+//     largest group keys; the smallest of these, b, is reached by at least k group keys, so by at
+//     least k values:
 //     the k-th largest value is >= b, and every survivor (x / T ties values just below the k-th
-//     one) is at or above the tie floor of b. Each warp re-reads its groups whose key reaches that
-//     floor (four groups per warp-wide load); their values at or above it are the candidates,
+//     one) is at or above the tie floor of b. The groups whose key reaches that floor are listed
+//     per warp and re-read by the whole CTA; their values at or above it are the candidates,
 //     settled exactly by f_settle.
 // For rows longer than GS_MAXG groups, pass 2 reads runs of `coarse` consecutive groups as one.
 
@@ -30,15 +31,20 @@
 #ifndef PB_GM_UNROLL
 #define PB_GM_UNROLL 8
 #endif
+#ifndef PB_GM_TPW
+#define PB_GM_TPW 0
+#endif
 constexpr int GM_GB = 128;                    // bytes per group
 constexpr int GM_GV = GM_GB / 16;             // 16-byte vectors per group
 constexpr int GM_THREADS = 256;
 constexpr int GM_WARPS = GM_THREADS / 32;
 constexpr int GM_MINB = PB_GM_MINB;           // CTAs per SM pass 1 is compiled for
 constexpr int GM_UNROLL = PB_GM_UNROLL;       // tasks each lane has in flight (128 KB per SM)
+// tasks per warp in CTAs of a fixed size (0: one wave of equal shares, measured fastest on B200)
+constexpr int GM_TPW = PB_GM_TPW;
 constexpr int GS_THREADS = 256;
 constexpr int GS_NW = GS_THREADS / 32;
-constexpr int GS_NPT = 16;                    // (coarse) group keys per thread, contiguous
+constexpr int GS_NPT = 16;                    // (coarse) group keys per thread, in runs of 4
 constexpr int GS_MAXG = GS_THREADS * GS_NPT;  // coarse groups a row is read as
 constexpr int GS_WCAP = 128;                  // groups one warp re-reads (more: the cluster kernel)
 constexpr int GS_RU = 4;                      // re-read vectors in flight per lane
@@ -99,9 +105,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_MINB) group_max_kernel(GroupArg
   const int lane = threadIdx.x & 31, sub = lane >> 3, part = lane & 7;
   const int64_t W = (int64_t)gridDim.x * GM_WARPS;
   const int64_t w = (int64_t)blockIdx.x * GM_WARPS + (threadIdx.x >> 5);
-  const int64_t t0 = w * g.ntasks / W, t1 = (w + 1) * g.ntasks / W;
   const int32_t ngr = g.ngr, ngs = g.ngs, nrows = (int32_t)g.n_rows, V = (int32_t)g.vocab;
   const uint64_t pol_in = l2_policy_evict_first(), pol_out = l2_policy_evict_last();
+  const int64_t t0 = w * g.ntasks / W, t1 = (w + 1) * g.ntasks / W;
   // this lane's group of task t is 4 t + sub: (row, j), advanced by 4 groups per task
   const int64_t gid = 4 * t0 + sub;
   int32_t row = (int32_t)(gid / ngr), j = (int32_t)(gid - (int64_t)row * ngr);
@@ -148,26 +154,43 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x)
   return x;
 }
 
-// Candidates of a warp's listed groups: the warp reads the coarse groups wl[0..ng) (R groups each)
-// 16 bytes per lane, GS_RU vectors per lane in flight; every value whose key reaches thr goes to L
-// (shared counter *n; entries past F_LCAP are counted, not stored). All 32 lanes call.
+// Candidates of the CTA's listed groups: warp w listed cnt[w] coarse groups (R groups each) at
+// lists + w * GS_WCAP; their 16-byte vectors are spread over all the CTA's threads, GS_RU per thread
+// in flight. Every value at or above thr_v (the value of the threshold key; the row holds no NaN)
+// goes to L (shared counter *n; entries past F_LCAP are counted, not stored). A vector whose largest
+// value is below thr_v is skipped whole.
 template <typename T>
-__device__ __forceinline__ void warp_candidates(const T* row, const uint32_t* wl, uint32_t ng, int32_t R, int64_t V,
-                                                uint32_t thr, uint64_t* L, uint32_t* n) {
+__device__ __forceinline__ void cta_candidates(const T* row, const uint32_t* lists, const uint32_t* cnt, int32_t R,
+                                               int64_t V, float thr_v, uint64_t* L, uint32_t* n) {
   constexpr int EPV = Elem<T>::EPV, GE = GM_GB / Elem<T>::ES;
-  const int lane = threadIdx.x & 31;
-  const uint32_t vpg = (uint32_t)R * GM_GV;  // vectors per coarse group
-  const uint32_t nv = ng * vpg;
-  for (uint32_t b0 = 0; b0 < nv; b0 += 32 * GS_RU) {
+  const uint32_t vpg = (uint32_t)R * GM_GV;
+  uint32_t start[GS_NW + 1];
+  start[0] = 0;
+#pragma unroll
+  for (int w = 0; w < GS_NW; ++w) start[w + 1] = start[w] + cnt[w] * vpg;
+  const uint32_t nv = start[GS_NW];
+  for (uint32_t b0 = 0; b0 < nv; b0 += GS_THREADS * GS_RU) {
     uint4 vv[GS_RU];
     int64_t ee[GS_RU];
 #pragma unroll
     for (int u = 0; u < GS_RU; ++u) {
-      const uint32_t vi = b0 + (uint32_t)(u * 32 + lane);
+      const uint32_t vi = b0 + (uint32_t)(u * GS_THREADS + threadIdx.x);
       ee[u] = -1;
       vv[u] = make_uint4(0u, 0u, 0u, 0u);
       if (vi < nv) {
-        const int64_t e = (int64_t)wl[vi / vpg] * R * GE + (int64_t)(vi % vpg) * EPV;
+        int w = 0;
+        uint32_t first = 0;
+#pragma unroll
+        for (int x = 1; x < GS_NW; ++x) {
+          if (vi >= start[x]) {
+            w = x;
+            first = start[x];
+          }
+        }
+        const uint32_t r = vi - first;  // vector r of warp w's list
+        const uint32_t gsel = (R == 1) ? (r >> 3) : r / vpg;
+        const uint32_t part = r - gsel * vpg;
+        const int64_t e = (int64_t)lists[w * GS_WCAP + gsel] * R * GE + (int64_t)part * EPV;
         if (e < V) {
           ee[u] = e;
           vv[u] = (e + EPV <= V) ? *reinterpret_cast<const uint4*>(row + e) : part_vec<T>(row + e, (int)(V - e));
@@ -176,27 +199,28 @@ __device__ __forceinline__ void warp_candidates(const T* row, const uint32_t* wl
     }
 #pragma unroll
     for (int u = 0; u < GS_RU; ++u) {
-      if (ee[u] < 0) continue;
+      if (ee[u] < 0 || !(vec_max<T>(vv[u]) >= thr_v)) continue;
       float x[EPV];
       Elem<T>::unpack(vv[u], x);
 #pragma unroll
       for (int q = 0; q < EPV; ++q) {
-        const uint32_t kx = key_of(x[q]);
-        if (kx >= thr && ee[u] + q < V) {
+        if (x[q] >= thr_v && ee[u] + q < V) {
           const uint32_t pos = atomicAdd(n, 1u);
-          if (pos < (uint32_t)F_LCAP) L[pos] = compose(kx, (uint32_t)(ee[u] + q));
+          if (pos < (uint32_t)F_LCAP) L[pos] = compose(key_of(x[q]), (uint32_t)(ee[u] + q));
         }
       }
     }
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
+// MINB: CTAs per SM the kernel is compiled for (2 for batches of up to two rows per SM; 4 for more
+// rows, which then take fewer waves).
+template <typename T, int MINB>
+__global__ void __launch_bounds__(GS_THREADS, MINB) group_settle_kernel(GroupArgs g) {
   constexpr int EPV = Elem<T>::EPV, GE = GM_GB / Elem<T>::ES;
   __shared__ uint64_t L[F_LCAP];
   __shared__ uint32_t s_list[GS_NW * GS_WCAP];
-  __shared__ uint32_t s_bound[GS_NW], s_max[GS_NW];
+  __shared__ uint32_t s_bound[GS_NW], s_max[GS_NW], s_cnt[GS_NW];
   __shared__ unsigned long long s_best[GS_NW];
   __shared__ uint32_t s_n;
 
@@ -227,7 +251,9 @@ __global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
       g.logits + (g.row_index ? (int64_t)g.row_index[item] : item) * g.row_stride_bytes);
   const int32_t ngr = g.ngr, R = g.coarse;
   const int32_t nc = (ngr + R - 1) / R;
-  const int32_t c0 = tid * GS_NPT;  // this thread's coarse groups: c0 .. c0 + GS_NPT - 1
+  // this thread's coarse groups: runs of 4, the CTA's threads side by side, so every warp holds keys
+  // from the whole row
+  auto cidx = [&](int i) -> int32_t { return ((i >> 2) * GS_THREADS + tid) * 4 + (i & 3); };
   griddep_wait();  // pass 1's group keys
   const uint32_t* gm = g.gmax + item * (int64_t)g.ngs;
   uint32_t val[GS_NPT];
@@ -236,7 +262,7 @@ __global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
 #pragma unroll
     for (int i = 0; i < GS_NPT; i += 4) {
       uint4 q = make_uint4(0u, 0u, 0u, 0u);
-      if (c0 + i < ngr) q = __ldcg(reinterpret_cast<const uint4*>(gm + c0 + i));
+      if (cidx(i) < ngr) q = __ldcg(reinterpret_cast<const uint4*>(gm + cidx(i)));
       val[i] = q.x;
       val[i + 1] = q.y;
       val[i + 2] = q.z;
@@ -244,11 +270,11 @@ __global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
     }
 #pragma unroll
     for (int i = 0; i < GS_NPT; ++i)
-      if (c0 + i >= nc) val[i] = 0;
+      if (cidx(i) >= nc) val[i] = 0;
   } else {
 #pragma unroll
     for (int i = 0; i < GS_NPT; ++i) {
-      const int32_t c = c0 + i;
+      const int32_t c = cidx(i);
       uint32_t x = 0;
       if (c < nc) {
         const int32_t e = min(ngr, (c + 1) * R);
@@ -263,7 +289,7 @@ __global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
     unsigned long long best = 0;
 #pragma unroll
     for (int i = 0; i < GS_NPT; ++i)
-      if (c0 + i < nc) best = max(best, (unsigned long long)compose(val[i], (uint32_t)(c0 + i)));
+      if (cidx(i) < nc) best = max(best, (unsigned long long)compose(val[i], (uint32_t)cidx(i)));
     best = warp_max_u64(best);
     if (lane == 0) s_best[warp] = best;
     __syncthreads();
@@ -293,33 +319,14 @@ __global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
     return;
   }
 
-  // top-k: the warp's cw-th largest group key (counted with multiplicity; padding keys are 0, below
-  // every key): cw rounds, each taking one holder of the warp's largest remaining key out
+  // top-k: the warp's cw-th largest lane maximum (each lane maximum is a group key, so at least cw of
+  // the warp's group keys reach it); padding keys are 0, below every key
   const int cw = (p.top_k + GS_NW - 1) / GS_NW;
-  uint32_t taken_mask = 0;  // bit i: val[i] taken out
   uint32_t lm = 0;
 #pragma unroll
   for (int i = 0; i < GS_NPT; ++i) lm = max(lm, val[i]);
-  uint32_t wmax = 0, kth = 0;
-  for (int r = 0; r < cw; ++r) {
-    kth = __reduce_max_sync(0xFFFFFFFFu, lm);
-    if (r == 0) wmax = kth;
-    const uint32_t holders = __ballot_sync(0xFFFFFFFFu, lm == kth);
-    if (lane == __ffs(holders) - 1) {
-      bool taken = false;
-      lm = 0;
-#pragma unroll
-      for (int i = 0; i < GS_NPT; ++i) {
-        const bool live = !((taken_mask >> i) & 1u);
-        if (live && !taken && val[i] == kth) {
-          taken_mask |= 1u << i;
-          taken = true;
-        } else if (live) {
-          lm = max(lm, val[i]);
-        }
-      }
-    }
-  }
+  const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, lm);
+  const uint32_t kth = warp_cth_largest(lm, cw);
   if (lane == 0) {
     s_bound[warp] = kth;
     s_max[warp] = wmax;
@@ -340,23 +347,27 @@ __global__ void __launch_bounds__(GS_THREADS) group_settle_kernel(GroupArgs g) {
   }
   const uint32_t thr = (bound > KEY_NEG_INF) ? key_of(tie_floor(value_of(bound), tf)) : 0u;
 
-  // each warp lists its lanes' groups whose key reaches thr and re-reads them together
+  // each warp lists its lanes' groups whose key reaches thr; then the CTA re-reads them together
   uint32_t* wl = s_list + warp * GS_WCAP;
   uint32_t cnt = 0;
 #pragma unroll
   for (int i = 0; i < GS_NPT; ++i) {
-    const bool hit = c0 + i < nc && val[i] >= thr;
+    const bool hit = cidx(i) < nc && val[i] >= thr;
     const uint32_t b = __ballot_sync(0xFFFFFFFFu, hit);
     const uint32_t pos = cnt + (uint32_t)__popc(b & lanemask_lt());
-    if (hit && pos < (uint32_t)GS_WCAP) wl[pos] = (uint32_t)(c0 + i);
+    if (hit && pos < (uint32_t)GS_WCAP) wl[pos] = (uint32_t)cidx(i);
     cnt += (uint32_t)__popc(b);
   }
-  __syncwarp();
-  if (cnt > (uint32_t)GS_WCAP) {
-    if (lane == 0) atomicAdd(&s_n, (uint32_t)F_LCAP + 1u);  // more groups than the list holds: retry
-  } else {
-    warp_candidates<T>(row, wl, cnt, R, V, thr, L, &s_n);
+  if (lane == 0) s_cnt[warp] = cnt;
+  __syncthreads();
+  bool over = false;
+#pragma unroll
+  for (int w = 0; w < GS_NW; ++w) over |= s_cnt[w] > (uint32_t)GS_WCAP;
+  if (over) {  // more groups than the lists hold: the cluster kernel
+    if (tid == 0) f_mark_retry(fa, item);
+    return;
   }
+  cta_candidates<T>(row, s_list, s_cnt, R, V, thr ? value_of(thr) : -INFINITY, L, &s_n);
   __syncthreads();
   if (warp != 0) return;
   const uint32_t n = s_n;

@@ -2563,7 +2563,8 @@ bool groups_eligible(const void* logits, int64_t row_stride, int es, int64_t n_r
   return (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && ((row_stride * es) & 15) == 0;
 }
 
-// Pass-1 grid: the CTAs that fit on the device at once (at least one task per warp).
+// Pass-1 grid: GM_TPW tasks per warp, or (GM_TPW = 0) the CTAs that fit on the device at once (at
+// least one task per warp).
 template <typename T>
 int64_t group_grid(int64_t ntasks) {
   static DeviceInt occ;
@@ -2577,6 +2578,7 @@ int64_t group_grid(int64_t ntasks) {
     occ.v[dev].store(per_sm, std::memory_order_relaxed);
   }
   const int64_t full = (int64_t)per_sm * sm_count();
+  if (GM_TPW > 0) return std::max<int64_t>(1, (ntasks + (int64_t)GM_TPW * GM_WARPS - 1) / ((int64_t)GM_TPW * GM_WARPS));
   return std::max<int64_t>(1, std::min<int64_t>(full, (ntasks + GM_WARPS - 1) / GM_WARPS));
 }
 
@@ -2611,7 +2613,9 @@ int run_groups(const Args& a, uint8_t* workspace, int es, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, group_settle_kernel<T>, g) != cudaSuccess) return PB_E_LAUNCH;
+  const cudaError_t e = (a.n_rows <= 2 * (int64_t)sm_count()) ? cudaLaunchKernelEx(&cfg, group_settle_kernel<T, 2>, g)
+                                                              : cudaLaunchKernelEx(&cfg, group_settle_kernel<T, 4>, g);
+  if (e != cudaSuccess) return PB_E_LAUNCH;
   if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
   Args c = a;
   c.complement = 1;

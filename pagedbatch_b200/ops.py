@@ -47,21 +47,55 @@ def pack_params(temperature, top_p, top_k, uniform, seeds=None, steps=None) -> n
     return rec
 
 
+GROUP_KMAX = 128  # largest top_k the two-pass launch of pb_sample_ws settles
+
+
+def group_rows(rec: np.ndarray) -> tuple[bool, int]:
+    """Whether every row is one the two-pass launch of pb_sample_ws settles itself (valid parameters,
+    greedy or 0 < top_k <= 128, a usable draw), and the largest top_k among them (which must also
+    stay below the vocabulary). Rows of other kinds go to the cluster kernel after both passes, so
+    a batch holding them runs faster through pb_sample."""
+    if rec.size == 0:
+        return False, 0
+    t, p, k = rec["temperature"], rec["top_p"], rec["top_k"]
+    valid = (t >= 0.0) & (p > 0.0) & (p <= 1.0) & (k >= 0)
+    greedy = t == 0.0
+    draw = ((rec["rng"] & _lib.RNG_PHILOX) != 0) | ((rec["uniform"] >= 0.0) & (rec["uniform"] < 1.0))
+    small = (k > 0) & (k <= GROUP_KMAX) & draw
+    ok = bool(np.all(valid & (greedy | small)))
+    kmax = int(k[~greedy].max()) if np.any(~greedy) else 0
+    return ok, kmax
+
+
+def mark_rows(params: torch.Tensor, rec: np.ndarray) -> torch.Tensor:
+    """Record on the device params tensor which launch suits its rows (read by the path choice)."""
+    params._pb_group_rows = group_rows(rec)
+    return params
+
+
 def params_tensor(rec: np.ndarray, device, pinned: bool = True) -> torch.Tensor:
     """Upload packed records: one pinned host buffer, one non-blocking H2D copy."""
     host = torch.from_numpy(rec.view(np.uint8).copy())
     if pinned:
         host = host.pin_memory()
-    return host.to(device, non_blocking=True)
+    return mark_rows(host.to(device, non_blocking=True), rec)
 
 
 _WS: dict = {}
 
 
-def _ws_path() -> bool:
-    """pb_sample (the default; measured faster at the benchmark's shapes) or, with PB_PATH=ws, tokens
-    without probabilities through pb_sample_ws (the balanced streaming launch over a workspace)."""
-    return os.environ.get("PB_PATH", "full") == "ws"
+def _ws_path(params: torch.Tensor | None = None, vocab: int = 0) -> bool:
+    """Whether tokens without probabilities go through pb_sample_ws (over a workspace) rather than
+    pb_sample. PB_PATH=ws / full (or cluster, stream: pb_sample's own choices) force one. By default
+    pb_sample_ws runs when the params tensor's rows all suit its two-pass launch (see group_rows;
+    measured on B200: [256, 128256] fp32 top-k rows 38 us against 41 us, [1024, 128256] bf16 85 us
+    against 100 us), and pb_sample otherwise (a batch with temperature-only or top-p-only rows: 137
+    us against 169 us)."""
+    env = os.environ.get("PB_PATH", "auto")
+    if env != "auto":
+        return env == "ws"
+    ok, kmax = getattr(params, "_pb_group_rows", (False, 0))
+    return ok and kmax < vocab
 
 
 def _workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
@@ -102,7 +136,7 @@ def _launch(logits: torch.Tensor, params: torch.Tensor, row_index, with_info: bo
     info = torch.empty((n, _lib.ROW_INFO.itemsize), dtype=torch.uint8, device=dev) if with_info else None
     probs = torch.empty((n, V), dtype=torch.float32, device=dev) if with_probs else None
     L = _lib.load()
-    if not with_probs and _ws_path():
+    if not with_probs and _ws_path(params, V):
         with torch.cuda.device(dev):
             need = L.pb_sample_ws_bytes(n, V, _DTYPE_CODE[logits.dtype])
             stream = torch.cuda.current_stream(dev).cuda_stream

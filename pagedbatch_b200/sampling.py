@@ -72,13 +72,13 @@ def _upload(rec: np.ndarray, rows: np.ndarray | None, device) -> tuple[torch.Ten
         host = torch.empty(pb.size, dtype=torch.uint8, pin_memory=True)
         host.numpy()[:] = pb
         dev = host.to(device, non_blocking=True)
-        return dev, None
+        return ops.mark_rows(dev, rec), None
     ri = rows.astype(np.int32).view(np.uint8)
     host = torch.empty(pb.size + ri.size, dtype=torch.uint8, pin_memory=True)
     host.numpy()[: pb.size] = pb
     host.numpy()[pb.size :] = ri
     dev = host.to(device, non_blocking=True)
-    return dev[: pb.size], dev[pb.size :].view(torch.int32)
+    return ops.mark_rows(dev[: pb.size], rec), dev[pb.size :].view(torch.int32)
 
 
 def launch_rows(

@@ -68,3 +68,32 @@ def test_huge_top_k_saturates():
     a top_k past int32 must pack (saturated), not raise."""
     rec = pack_rows([SamplingParams(temperature=1.0, top_k=2**40)], np.array([0.5]))
     assert rec["top_k"][0] == 2**31 - 1
+
+
+def test_workspace_path_choice(monkeypatch):
+    """The ops layer sends a batch to pb_sample_ws only when every row suits its two-pass launch
+    (greedy, or 0 < top_k <= 128 below the vocabulary, valid parameters, a usable draw), unless
+    PB_PATH forces a path."""
+    import oracle
+    from pagedbatch_b200 import ops
+
+    monkeypatch.delenv("PB_PATH", raising=False)
+
+    def choice(t, p, k, u, vocab=1000, rec=None):
+        rec = oracle.make_params(t, p, k, u) if rec is None else rec
+        return ops._ws_path(ops.mark_rows(torch.empty(0), rec), vocab)
+
+    assert choice([0.7, 0.0, 1.0], [0.95, 1.0, 0.5], [50, 0, 128], [0.3, 0.1, 0.0])
+    assert not choice([0.7, 1.0], [0.95, 1.0], [50, 0], [0.3, 0.1])  # temperature-only row
+    assert not choice([0.7, 1.0], [0.95, 0.9], [50, 129], [0.3, 0.1])  # top_k above 128
+    assert not choice([0.7], [0.95], [50], [0.3], vocab=50)  # top_k not below the vocabulary
+    assert not choice([0.7], [0.95], [50], [1.0])  # a draw outside [0, 1)
+    assert not choice([-1.0], [0.95], [50], [0.3])  # rejected parameters
+    assert not choice([], [], [], [])
+    dev_rec = oracle.make_device_rng_params([0.7, 0.0], [0.9, 1.0], [20, 0], [5, 6], [0, 3])
+    assert choice(None, None, None, None, rec=dev_rec)
+    assert not ops._ws_path(torch.empty(0), 1000)  # a params tensor made elsewhere: pb_sample
+    monkeypatch.setenv("PB_PATH", "full")
+    assert not choice([0.7], [0.95], [50], [0.3])
+    monkeypatch.setenv("PB_PATH", "ws")
+    assert choice([0.7, 1.0], [0.95, 1.0], [50, 0], [0.3, 0.1])

@@ -27,7 +27,7 @@ pytestmark = pytest.mark.gpu
 def _env(cuda):
     os.environ["PB_PATH"] = "stream"  # whatever the batch size, the streaming kernel goes first
     yield
-    for k in ("PB_PATH", "PB_TEST_STAGE_POLLS", "PB_NO_PDL"):
+    for k in ("PB_PATH", "PB_WS", "PB_TEST_STAGE_POLLS", "PB_NO_PDL"):
         os.environ.pop(k, None)
 
 
@@ -166,6 +166,7 @@ def test_balanced_bounded_wait_gives_up_and_reports_timeout():
     CTA gave up still arrives (with a timed-out record), so every split row reports PB_ROW_TIMEOUT,
     its arrival counter completes, and the next call (normal waits) over the same workspace is right."""
     os.environ["PB_PATH"] = "ws"
+    os.environ["PB_WS"] = "balanced"  # the balanced streaming launch (the two-pass launch never waits)
     w = workloads.config1(rows=64)
     rec = rec_for(w.params, w.uniforms())
     x = w.logits.cuda()
