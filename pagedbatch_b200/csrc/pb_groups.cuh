@@ -22,7 +22,7 @@
 //     the k-th largest value is >= b, and every survivor (x / T ties values just below the k-th
 //     one) is at or above the tie floor of b. The groups whose key reaches that floor are listed
 //     per warp and re-read by the whole CTA; their values at or above it are the candidates,
-//     settled exactly by f_settle.
+//     settled exactly by f_settle in one warp.
 // For rows longer than GS_MAXG groups, pass 2 reads runs of `coarse` consecutive groups as one.
 
 #ifndef PB_GM_MINB
@@ -107,6 +107,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_MINB) group_max_kernel(GroupArg
   const int64_t w = (int64_t)blockIdx.x * GM_WARPS + (threadIdx.x >> 5);
   const int32_t ngr = g.ngr, ngs = g.ngs, nrows = (int32_t)g.n_rows, V = (int32_t)g.vocab;
   const uint64_t pol_in = l2_policy_evict_first(), pol_out = l2_policy_evict_last();
+  // let pass 2 launch now: its CTAs take the SMs this pass frees and wait (griddepcontrol.wait)
+  // until the whole pass has finished and its stores are visible
+  griddep_launch_dependents();
   const int64_t t0 = w * g.ntasks / W, t1 = (w + 1) * g.ntasks / W;
   // this lane's group of task t is 4 t + sub: (row, j), advanced by 4 groups per task
   const int64_t gid = 4 * t0 + sub;
@@ -145,7 +148,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_MINB) group_max_kernel(GroupArg
       if (part == 0 && at[u] >= 0) st_keep_u32(g.gmax + at[u], k, pol_out);
     }
   }
-  griddep_launch_dependents();
 }
 
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x) {
@@ -197,17 +199,32 @@ __device__ __forceinline__ void cta_candidates(const T* row, const uint32_t* lis
         }
       }
     }
+    // this thread's candidates: a bit per element of each vector; one shared atomic per warp
+    uint32_t mask[GS_RU];
+    uint32_t mine = 0;
 #pragma unroll
     for (int u = 0; u < GS_RU; ++u) {
-      if (ee[u] < 0 || !(vec_max<T>(vv[u]) >= thr_v)) continue;
-      float x[EPV];
-      Elem<T>::unpack(vv[u], x);
+      mask[u] = 0;
+      if (ee[u] >= 0 && vec_max<T>(vv[u]) >= thr_v) {
+        float x[EPV];
+        Elem<T>::unpack(vv[u], x);
 #pragma unroll
-      for (int q = 0; q < EPV; ++q) {
-        if (x[q] >= thr_v && ee[u] + q < V) {
-          const uint32_t pos = atomicAdd(n, 1u);
-          if (pos < (uint32_t)F_LCAP) L[pos] = compose(key_of(x[q]), (uint32_t)(ee[u] + q));
-        }
+        for (int q = 0; q < EPV; ++q)
+          if (x[q] >= thr_v && ee[u] + q < V) mask[u] |= 1u << q;
+      }
+      mine += (uint32_t)__popc(mask[u]);
+    }
+    const uint32_t incl = warp_incl_scan(mine);
+    uint32_t base = 0;
+    if ((threadIdx.x & 31) == 31 && incl) base = atomicAdd(n, incl);
+    base = __shfl_sync(0xFFFFFFFFu, base, 31) + incl - mine;
+#pragma unroll
+    for (int u = 0; u < GS_RU; ++u) {
+      while (mask[u]) {
+        const int q = __ffs(mask[u]) - 1;
+        mask[u] &= mask[u] - 1;
+        if (base < (uint32_t)F_LCAP) L[base] = compose(key_of(Elem<T>::elem(vv[u], q)), (uint32_t)(ee[u] + q));
+        ++base;
       }
     }
   }
@@ -369,8 +386,8 @@ __global__ void __launch_bounds__(GS_THREADS, MINB) group_settle_kernel(GroupArg
   }
   cta_candidates<T>(row, s_list, s_cnt, R, V, thr ? value_of(thr) : -INFINITY, L, &s_n);
   __syncthreads();
-  if (warp != 0) return;
   const uint32_t n = s_n;
+  if (warp != 0) return;
   if (n == 0 || n > (uint32_t)F_LCAP || !f_settle(fa, p, item, L, (int)n, m)) {
     if (lane == 0) f_mark_retry(fa, item);
   }
