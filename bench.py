@@ -312,6 +312,7 @@ def measure_vocab_parallel(world, rank, local, dist, steps: int, warmup: int):
     B, V = w.logits.shape
     lo, hi = V * rank // world, V * (rank + 1) // world
     xs = [w.logits[:, lo:hi].contiguous().to(dev) for _ in range(NROT)]
+    xs_ptr = xs[0].data_ptr()
     rec = sampling.pack_rows(w.params, np.array(w.uniforms()))
     dparams = ops.params_tensor(rec, dev)
     cap = record_cap(w.params)
@@ -388,8 +389,10 @@ def measure_vocab_parallel(world, rank, local, dist, steps: int, warmup: int):
         "record_bytes_per_row": rb, "all_gather_bytes_per_rank": B * rb,
         "fallback_rows": fallback,
         "shard_hbm_frac": shard_bytes / (step_ms / 1e3) / 1e9 / peak,
-        "kernels": f"pb_candidates ({L.pb_sample_launches(B, hi - lo, 1, 0)} launch(es)) + NCCL all_gather_into_tensor "
-                   "+ pb_merge (1 launch)",
+        "kernels": (f"pb_candidates_ws ({L.pb_sample_ws_launches(xs_ptr, B, hi - lo, hi - lo, 1)} launches)"
+                    if ops._ws_path(dparams, hi - lo) else
+                    f"pb_candidates ({L.pb_sample_launches(B, hi - lo, 1, 0)} launch(es))")
+                   + " + NCCL all_gather_into_tensor + pb_merge (1 launch)",
         "timing": "eager launches between CUDA events, max over ranks; per-phase medians from rank 0",
         "clocks": clk.summary(),
     }

@@ -213,6 +213,19 @@ PB_API int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t 
                          void* out_records, void* stream);
 
 /*
+ * pb_candidates over a caller workspace: the same records (no counterpart in the reference). For
+ * shards whose rows start on 16-byte boundaries it runs the two-pass launch of pb_sample_ws in shard
+ * mode (a streaming pass over the shard's group keys, then one CTA per row writing the row's
+ * record, the cluster kernel for the rows it leaves); otherwise, or with a workspace smaller than
+ * pb_candidates_ws_bytes(n_rows, shard_vocab, dtype), pb_candidates' own launches. workspace:
+ * 256-byte aligned device memory of any content, not used by another call while this one runs.
+ */
+PB_API int64_t pb_candidates_ws_bytes(int64_t n_rows, int64_t shard_vocab, int dtype);
+PB_API int pb_candidates_ws(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t row_stride,
+                            const int32_t* row_index, const pb_row_params* params, int64_t vocab_offset,
+                            int32_t cap, void* out_records, void* workspace, int64_t ws_bytes, void* stream);
+
+/*
  * Merge: records laid out [n_shards][n_rows][pb_record_bytes(cap)], shards in column order.
  * Writes out_token (-1 unless PB_ROW_OK) and optional out_info exactly as pb_sample would for the
  * full rows, except PB_ROW_FALLBACK rows.

@@ -57,6 +57,8 @@ EXPORTS = (
     "pb_sample_ws",
     "pb_sample_ws_bytes",
     "pb_sample_ws_launches",
+    "pb_candidates_ws",
+    "pb_candidates_ws_bytes",
     "pb_sample_noalloc",
     "pb_sample_noalloc_max_bytes",
     "pb_candidates",
@@ -107,6 +109,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     L.pb_sample_ws_bytes.restype = i64
     L.pb_sample_ws_launches.argtypes = [vp, i64, i64, i64, i32]
     L.pb_sample_ws_launches.restype = i32
+    L.pb_candidates_ws.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, i32, vp, vp, i64, vp]
+    L.pb_candidates_ws.restype = i32
+    L.pb_candidates_ws_bytes.argtypes = [i64, i64, i32]
+    L.pb_candidates_ws_bytes.restype = i64
     L.pb_candidates.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, i32, vp, vp]
     L.pb_candidates.restype = i32
     L.pb_merge.argtypes = [vp, i32, i64, i32, vp, vp, vp, vp]

@@ -24,6 +24,8 @@
 //     per warp and re-read by the whole CTA; their values at or above it are the candidates,
 //     settled exactly by f_settle in one warp.
 // For rows longer than GS_MAXG groups, pass 2 reads runs of `coarse` consecutive groups as one.
+// In shard mode (vocabulary-parallel, cand_out set) pass 2 writes each row's candidate record (its
+// survivors with global indices, or its first maximum) exactly as the streaming kernel does.
 
 #ifndef PB_GM_MINB
 #define PB_GM_MINB 4
@@ -64,6 +66,10 @@ struct GroupArgs {
   int32_t ngs;     // row stride of gmax: ngr rounded up to a multiple of 4
   int32_t coarse;  // groups per coarse group in pass 2: ceil(ngr / GS_MAXG)
   int64_t ntasks;  // ceil(n_rows * ngr / 4); n_rows * ngs < 2^31
+  // vocabulary-parallel shard mode: per-row candidate records instead of tokens (else null)
+  uint8_t* cand_out;
+  int32_t cand_cap;
+  int64_t vocab_offset;
 };
 
 __device__ __forceinline__ uint4 ld_once16(const void* p, uint64_t pol) {
@@ -257,9 +263,9 @@ __global__ void __launch_bounds__(GS_THREADS, MINB) group_settle_kernel(GroupArg
   fa.params = g.params;
   fa.out_token = g.out_token;
   fa.out_info = g.out_info;
-  fa.cand_out = nullptr;
-  fa.cand_cap = 0;
-  fa.vocab_offset = 0;
+  fa.cand_out = g.cand_out;
+  fa.cand_cap = g.cand_cap;
+  fa.vocab_offset = g.vocab_offset;
   fa.poll_limit = 0;
   fa.balanced = 0;
   fa.row_cnt = nullptr;

@@ -2600,6 +2600,9 @@ int run_groups(const Args& a, uint8_t* workspace, int es, cudaStream_t st) {
   g.ngs = (int32_t)gp.ngs;
   g.coarse = (int32_t)gp.coarse;
   g.ntasks = gp.ntasks;
+  g.cand_out = a.cand_out;
+  g.cand_cap = a.cand_cap;
+  g.vocab_offset = a.vocab_offset;
   group_max_kernel<T><<<(unsigned)group_grid<T>(gp.ntasks), GM_THREADS, 0, st>>>(g);
   if (cudaGetLastError() != cudaSuccess) return PB_E_LAUNCH;
   const bool pdl = getenv("PB_NO_PDL") == nullptr;
@@ -2622,6 +2625,12 @@ int run_groups(const Args& a, uint8_t* workspace, int es, cudaStream_t st) {
   return launch<T>(c, cluster_size_for(a.n_rows, a.vocab, es), st, pdl);
 }
 
+int run_groups_args(const Args& a, int dtype, int es, uint8_t* workspace, cudaStream_t st) {
+  if (dtype == PB_DTYPE_F32) return run_groups<float>(a, workspace, es, st);
+  if (dtype == PB_DTYPE_BF16) return run_groups<__nv_bfloat16>(a, workspace, es, st);
+  return run_groups<__half>(a, workspace, es, st);
+}
+
 int run_groups_dtype(const void* logits, int dtype, int es, int64_t n_rows, int64_t vocab, int64_t row_stride,
                      const int32_t* row_index, const pb_row_params* params, int64_t* out_token,
                      pb_row_info* out_info, uint8_t* workspace, cudaStream_t st) {
@@ -2640,9 +2649,7 @@ int run_groups_dtype(const void* logits, int dtype, int es, int64_t n_rows, int6
   a.cand_out = nullptr;
   a.cand_cap = 0;
   a.vocab_offset = 0;
-  if (dtype == PB_DTYPE_F32) return run_groups<float>(a, workspace, es, st);
-  if (dtype == PB_DTYPE_BF16) return run_groups<__nv_bfloat16>(a, workspace, es, st);
-  return run_groups<__half>(a, workspace, es, st);
+  return run_groups_args(a, dtype, es, workspace, st);
 }
 
 // ---- allocation-free entry point -------------------------------------------------------------
@@ -2806,6 +2813,48 @@ int pb_candidates(const void* logits, int dtype, int64_t n_rows, int64_t shard_v
   a.cand_cap = cap;
   a.vocab_offset = vocab_offset;
   return run_rows_dtype(a, dtype, es, static_cast<cudaStream_t>(stream));
+}
+
+int64_t pb_candidates_ws_bytes(int64_t n_rows, int64_t shard_vocab, int dtype) {
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es || n_rows < 0 || shard_vocab <= 0) return PB_E_INVALID;
+  return group_plan(n_rows, shard_vocab, es).bytes;
+}
+
+int pb_candidates_ws(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t row_stride,
+                     const int32_t* row_index, const pb_row_params* params, int64_t vocab_offset, int32_t cap,
+                     void* out_records, void* workspace, int64_t ws_bytes, void* stream) {
+  if (n_rows < 0 || shard_vocab <= 0 || row_stride < shard_vocab || vocab_offset < 0) return PB_E_INVALID;
+  if (cap < 1 || cap > PB_CAND_MAX_CAP) return PB_E_INVALID;
+  if (vocab_offset + shard_vocab >= PB_MAX_VOCAB) return PB_E_TOO_LARGE;
+  if (n_rows == 0) return PB_OK;
+  if (!logits || !params || !out_records || !workspace) return PB_E_INVALID;
+  if (n_rows > (int64_t)(0x7FFFFFFF / 8)) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(out_records) & 15) != 0) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return PB_E_INVALID;
+  const int es = (dtype == PB_DTYPE_F32) ? 4 : (dtype == PB_DTYPE_BF16 || dtype == PB_DTYPE_F16) ? 2 : 0;
+  if (!es) return PB_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(logits) % es) != 0) return PB_E_INVALID;
+  if (!groups_eligible(logits, row_stride, es, n_rows, shard_vocab) ||
+      ws_bytes < group_plan(n_rows, shard_vocab, es).bytes)  // pb_candidates' launches
+    return pb_candidates(logits, dtype, n_rows, shard_vocab, row_stride, row_index, params, vocab_offset, cap,
+                         out_records, stream);
+  Args a;
+  a.logits = static_cast<const char*>(logits);
+  a.n_rows = n_rows;
+  a.vocab = shard_vocab;
+  a.row_stride = row_stride;
+  a.row_index = row_index;
+  a.params = params;
+  a.out_token = nullptr;
+  a.out_info = nullptr;
+  a.out_probs = nullptr;
+  a.only_fallback = nullptr;
+  a.complement = 0;
+  a.cand_out = static_cast<uint8_t*>(out_records);
+  a.cand_cap = cap;
+  a.vocab_offset = vocab_offset;
+  return run_groups_args(a, dtype, es, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 int pb_merge(const void* records, int32_t n_shards, int64_t n_rows, int32_t cap, const pb_row_params* params,

@@ -51,11 +51,23 @@ class CudaKernels:
         L = _lib.load()
         B, V = logits.shape
         rec = torch.empty((B, _lib.record_bytes(cap)), dtype=torch.uint8, device=logits.device)
+        code = ops._DTYPE_CODE[logits.dtype]
         with torch.cuda.device(logits.device):
+            stream = torch.cuda.current_stream(logits.device).cuda_stream
+            if ops._ws_path(dparams, V):
+                # every row suits the two passes (see ops.group_rows): pb_candidates over a workspace
+                need = L.pb_candidates_ws_bytes(B, V, code)
+                ws = ops._workspace(logits.device, stream, need)
+                rc = L.pb_candidates_ws(
+                    ctypes.c_void_p(logits.data_ptr()), code, B, V, logits.stride(0), None,
+                    ctypes.c_void_p(dparams.data_ptr()), int(vocab_offset), int(cap), ctypes.c_void_p(rec.data_ptr()),
+                    ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(stream))
+                _lib.check(rc, "pb_candidates_ws")
+                return rec
             rc = L.pb_candidates(
-                ctypes.c_void_p(logits.data_ptr()), ops._DTYPE_CODE[logits.dtype], B, V, logits.stride(0), None,
+                ctypes.c_void_p(logits.data_ptr()), code, B, V, logits.stride(0), None,
                 ctypes.c_void_p(dparams.data_ptr()), int(vocab_offset), int(cap), ctypes.c_void_p(rec.data_ptr()),
-                ctypes.c_void_p(torch.cuda.current_stream(logits.device).cuda_stream))
+                ctypes.c_void_p(stream))
         _lib.check(rc, "pb_candidates")
         return rec
 

@@ -426,3 +426,39 @@ def test_power_of_two_temperatures_cooperative_path(dtype):
     p = [1.0, 0.9, 1.0, 0.95, 0.5, 1.0, 0.99, 1.0, 1.0, 0.9, 0.7, 0.8]
     u = np.random.default_rng(5).random(B)
     compare(x, oracle.make_params(t, p, [0] * B, u), label=f"pow2 T {dtype}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_shard_records_two_pass_launch(dtype):
+    """Vocabulary-parallel records from the two-pass launch (pb_candidates_ws) on column slices of
+    the same GPU, merged with pb_merge: the same tokens and row info as pb_sample on the full rows,
+    for 2 and 4 slices, greedy and top-k rows (the path the ops layer takes when every row suits it),
+    and rows it hands to the cluster kernel (NaN, +inf)."""
+    from pagedbatch_b200.vocab_parallel import CudaKernels, record_cap
+
+    w = workloads.config3(rows=96)
+    x = w.logits.to(dtype)
+    x[5, 1000] = float("nan")
+    x[6, 70000] = float("inf")
+    params = list(w.params)
+    params[7] = type(params[7])(temperature=0.0, top_p=1.0, top_k=0)
+    rec = rec_for(params, w.uniforms())
+    dev = x.cuda()
+    dparams = ops.params_tensor(rec, dev.device)
+    B, V = x.shape
+    assert ops._ws_path(dparams, V // 4)
+    kern = CudaKernels()
+    cap = record_cap(params)
+    full_tok, full_info, _ = run_gpu(dev, rec, probs=False)
+    for n in (2, 4):
+        cuts = [V * r // n for r in range(n + 1)]
+        assert all((c * x.element_size()) % 16 == 0 for c in cuts)
+        recs = [kern.candidates(dev[:, cuts[r]:cuts[r + 1]].contiguous(), dparams, cuts[r], cap) for r in range(n)]
+        tok, info = kern.merge(torch.stack(recs), dparams, cap)
+        inf = ops.info_records(info)
+        ok = inf["status"] != _lib.ROW_FALLBACK
+        assert ok[:5].all() and ok[8:].all()
+        t = tok.cpu().numpy()
+        assert np.array_equal(t[ok], full_tok[ok]), f"{n} slices: tokens differ"
+        for f in INFO_FIELDS:
+            assert np.array_equal(inf[f][ok], full_info[f][ok]), f"{n} slices: info.{f} differs"
